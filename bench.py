@@ -1,0 +1,428 @@
+"""Benchmark of the RAC rotation-accumulate hot path on B200.
+
+Default workload (the headline metric): rac_matmul, fp32 row-major
+M = N = K = 4096, A and B i.i.d. U[-1, 1), CORDIC mode, 16 iterations.
+Metric: MAC-equivalent GOP/s = 2*M*N*K / t, summed over all ranks.  With N
+GPUs the columns of B and C are sharded across ranks (no collective on the
+data path; strong scaling of the fixed 4096^3 problem).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload matmul|rotate|rope|softmax|rmsnorm|layernorm|llama]
+
+`--impl reference` times the reference's own CPU implementation of
+rac_matmul (lib/c rac_hal_sgemm, AVX2, all host threads) built from its
+sources into oracle/_ref, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_peaks() -> dict:
+    try:
+        with open(PEAKS_PATH) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def load_traffic() -> dict:
+    try:
+        with open(TRAFFIC_PATH) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+# ── distributed plumbing ──────────────────────────────────────────────────
+
+def dist_init():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ── clocks ────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    """Samples nvidia-smi every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        mhz, maxm, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxm = max(maxm, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": maxm or None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ── CPU baselines (oracle/, the reference's lib/c built from its sources) ─
+
+def cpu_matmul_baseline(M: int, N: int, K: int, iters: int, reps: int = 1, warm: int = 1) -> dict:
+    """Times the reference's CPU rac_matmul (lib/c rac_hal_sgemm, AVX2 + OpenMP)
+    on the full problem, plus the CORDIC GEMM composed from the reference's
+    rac_project_n on a row sample (information only)."""
+    import numpy as np
+    import oracle as O
+    rng = np.random.default_rng(1)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    cores = os.cpu_count() or 1
+    out = {"cores": int(os.environ.get("OMP_NUM_THREADS", cores))}
+    if O.ref_available():
+        for _ in range(warm):
+            O.ref_sgemm(A, B)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            O.ref_sgemm(A, B)
+            ts.append(time.perf_counter() - t0)
+        t = statistics.mean(ts)
+        out.update(kind="reference", value=2.0 * M * N * K / t / 1e9,
+                   sample=f"full {M}x{N}x{K} rac_hal_sgemm (lib/c AVX2 FMA path), mean of {reps}")
+        rows = 16
+        t0 = time.perf_counter()
+        O.gemm_composed_ref(A[:rows], B, iters)
+        tc = time.perf_counter() - t0
+        out["cordic_composed"] = {"value": 2.0 * rows * N * K / tc / 1e9, "unit": "GOP/s",
+                                  "sample": f"{rows} rows of C, sum_k rac_project_n(.., {iters}) * |b|"}
+    else:
+        rows = 64
+        t0 = time.perf_counter()
+        O.gemm(A[:rows], B, "nn", 1, iters)
+        t = time.perf_counter() - t0
+        out.update(kind="port", value=2.0 * rows * N * K / t / 1e9,
+                   sample=f"{rows} rows of C through oracle.gemm (CORDIC, {iters} iterations)")
+    out["unit"] = "GOP/s"
+    return out
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's own CPU rac_matmul on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M = N = K = 4096
+    import numpy as np
+    import oracle as O
+    cores = os.cpu_count() or 1
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/librac_ref.so not built"}))
+        return
+    rng = np.random.default_rng(1)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    for _ in range(args.warmup):
+        O.ref_sgemm(A, B)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.ref_sgemm(A, B)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.mean(ts)
+    v = 2.0 * M * N * K / t / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": "rac_matmul MAC-equiv GOP/s at 4096^3", "value": v,
+        "unit": "GOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "rac_matmul 4096x4096x4096 fp32 U[-1,1) (reference lib/c CPU path)"},
+        "cpu_baseline": {"value": v, "unit": "GOP/s", "cores": cores, "kind": "reference",
+                         "sample": "full 4096^3 per step: lib/c rac_hal_sgemm -> rac_sgemm_avx2 "
+                                   "(the reference's CPU rac_matmul; FMA, lib/c has no CORDIC GEMM)"},
+        "e2e": {"value": v, "unit": "GOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ── GPU workloads ─────────────────────────────────────────────────────────
+
+def roofline_fp32(achieved_gops: float, iters: int, peaks: dict, sms: int, dur_ms: float,
+                  traffic) -> dict:
+    """FP32-issue roofline of the CORDIC GEMM: (2n+2) FP32 instructions per MAC
+    at SMs x 128 lanes x max SM clock (the cost model stated for the path)."""
+    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    instr_peak = sms * 128 * mhz * 1e6
+    peak_gops = 2.0 * instr_peak / (2 * iters + 2) / 1e9
+    return {"bound": "fp32_issue", "achieved": achieved_gops, "peak": peak_gops,
+            "unit": "GOP/s (MAC-equiv)", "frac": achieved_gops / peak_gops,
+            "peak_basis": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz / {2 * iters + 2} instr per MAC "
+                          "(of measured sm_max_mhz)",
+            "kernel_ms": dur_ms, "traffic": traffic}
+
+
+def run_matmul(args, world, rank, local) -> dict | None:
+    import torch
+    from rac_b200 import _lib, ext
+    M = N = K = args.size
+    iters = args.iters
+    mode = 0 if args.mode == "fast" else 1
+    n0, n1 = N * rank // world, N * (rank + 1) // world
+    Nl = n1 - n0
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    A = torch.rand((M, K), device=dev, generator=g) * 2 - 1
+    g.manual_seed(4321 + rank)
+    B = torch.rand((K, Nl), device=dev, generator=g) * 2 - 1
+    C = torch.empty((M, Nl), device=dev)
+    flush = torch.empty(256 << 20 >> 2, device=dev)    # 256 MiB > 126 MB L2
+    s = torch.cuda.current_stream()
+
+    def step():
+        ext.gemm(A, B, _lib.LAYOUT_NN, iters, mode, out=C, variant=args.variant)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()                              # between steps, outside the events
+            starts[i].record(s)
+            step()
+            ends[i].record(s)
+        torch.cuda.synchronize()
+    barrier(world)
+    per = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    t_local = statistics.mean(per)
+    t = max_over_ranks(t_local, world)
+    value = 2.0 * M * N * K / (t * 1e-3) / 1e9
+    achieved_local = 2.0 * M * Nl * K / (t_local * 1e-3) / 1e9
+
+    # e2e through the C ABI (rac_matmul_ex) with pinned host buffers.
+    Ah = A.cpu().pin_memory()
+    Bh = B.cpu().pin_memory()
+    Ch = torch.empty((M, Nl)).pin_memory()
+    L = _lib.lib()
+    e2e_steps = max(1, min(args.steps, 5))
+    L.rac_matmul_ex(Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr(), M, Nl, K, iters, mode)
+    _lib.check()
+    barrier(world)
+    ts = []
+    for _ in range(e2e_steps):
+        t0 = time.perf_counter()
+        L.rac_matmul_ex(Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr(), M, Nl, K, iters, mode)
+        ts.append(time.perf_counter() - t0)
+    _lib.check()
+    te = max_over_ranks(statistics.mean(ts), world)
+    assert torch.equal(Ch, C.cpu()), "e2e result differs from the device-resident run"
+
+    if rank != 0:
+        return None
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peaks = load_peaks()
+    traffic = load_traffic().get(f"gemm_cordic{iters}_{M}")
+    out = {
+        "metric": "rac_matmul MAC-equiv GOP/s at 4096^3" if M == 4096 else f"rac_matmul MAC-equiv GOP/s at {M}^3",
+        "value": value, "unit": "GOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"rac_matmul {M}x{N}x{K} fp32 U[-1,1), "
+                               f"{'CORDIC ' + str(iters) + ' iterations' if mode else 'FAST'}",
+                   "sharding": f"N-columns over {world} rank(s), no collective",
+                   "l2": "flushed between steps (256 MiB write outside the timed events)"},
+        "roofline": roofline_fp32(achieved_local, iters, peaks, sms, t_local, traffic),
+        "e2e": {"value": 2.0 * M * N * K / te / 1e9, "unit": "GOP/s",
+                "h2d_bytes_per_step": 4 * (M * K + K * Nl), "d2h_bytes_per_step": 4 * M * Nl,
+                "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    return out
+
+
+def run_stream(args, world, rank, local) -> dict | None:
+    """HBM-bound ops of the path (replicas across ranks: rows are independent)."""
+    import torch
+    from rac_b200 import ext
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    w = args.workload
+    if w == "rotate":
+        n = 1 << 26
+        v = torch.randn((n, 2), device=dev, generator=g)
+        th = (torch.rand(n, device=dev, generator=g) * 2 - 1) * 3.14159265
+        fn = lambda: ext.rotate_batch(v, th, args.iters)          # noqa: E731
+        bytes_, units, unit_name = 20 * n, n, "Gvec/s"
+        cfg = f"rac_rotate_batch_n 2^26 float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
+    elif w == "rope":
+        q = torch.randn((8, 32, 4096, 128), device=dev, generator=g)
+        c, s = ext.rope_cache(4096, 128, 10000.0, device=dev)
+        fn = lambda: ext.rope_apply_(q, c, s)                     # noqa: E731
+        bytes_, units, unit_name = 8 * q.numel(), q.numel(), "Gelem/s"
+        cfg = "rac_rope_apply Q [8,32,4096,128] fp32 in place, base 1e4"
+    elif w == "softmax":
+        x = torch.randn((32768, 4096), device=dev, generator=g) * 3
+        y = torch.empty_like(x)
+        fn = lambda: ext.softmax(x, out=y)                        # noqa: E731
+        bytes_, units, unit_name = 8 * x.numel(), x.numel(), "Gelem/s"
+        cfg = "rac_softmax [32768, 4096] fp32 ~N(0,9)"
+    else:
+        x = torch.randn((16384, 4096), device=dev, generator=g)
+        gam = torch.rand(4096, device=dev, generator=g) + 0.5
+        bet = torch.randn(4096, device=dev, generator=g) * 0.1
+        if w == "rmsnorm":
+            fn = lambda: ext.rmsnorm(x, gam, 1e-6)                # noqa: E731
+        else:
+            fn = lambda: ext.layernorm(x, gam, bet, 1e-6)         # noqa: E731
+        bytes_, units, unit_name = 8 * x.numel(), x.numel(), "Gelem/s"
+        cfg = f"rac_{w} [16384, 4096] fp32, eps 1e-6"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    flush = torch.empty(256 << 20 >> 2, device=dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    s = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(s)
+            fn()
+            ends[i].record(s)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
+    t = max_over_ranks(t_local, world)
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    ach = bytes_ / (t_local * 1e-3) / 1e9
+    return {
+        "metric": f"{w} throughput", "value": units * world / (t * 1e-3) / 1e9, "unit": unit_name,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": cfg, "sharding": "replicas",
+                                        "l2": "flushed between steps"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                     "frac": ach / peak, "peak_basis": "of measured" if "hbm_gbs" in peaks else "of fallback",
+                     "frac_of_8TBs": ach / 8000.0, "kernel_ms": t_local,
+                     "traffic": load_traffic().get(f"{w}")},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="matmul",
+                    choices=["matmul", "rotate", "rope", "softmax", "rmsnorm", "layernorm", "llama"])
+    ap.add_argument("--size", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=16)
+    ap.add_argument("--mode", choices=["cordic", "fast"], default="cordic")
+    ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world, rank, local = dist_init()
+    if args.workload == "matmul":
+        out = run_matmul(args, world, rank, local)
+    elif args.workload == "llama":
+        from rac_b200 import tp
+        out = tp.bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
+    else:
+        out = run_stream(args, world, rank, local)
+    if rank == 0 and out is not None:
+        if world == 1 and not args.no_cpu_baseline and args.workload == "matmul":
+            out["cpu_baseline"] = cpu_matmul_baseline(args.size, args.size, args.size, args.iters)
+        print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,337 @@
+"""CPU oracle for the RAC hot path -- TEST INFRASTRUCTURE ONLY.
+
+Two checkers live here:
+
+* ``orc``: the C restatement in ``rac_oracle.c`` (liborc.so), each function
+  citing the reference routine it follows.
+* ``ref``: the reference's own ``lib/c`` compiled from its sources by
+  ``oracle/Makefile`` into ``oracle/_ref/librac_ref.so`` (absent when it was
+  never built; the GPU box receives the prebuilt file).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py``
+import this package; the ``rac_b200`` product never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORC_PATH = os.path.join(HERE, "liborc.so")
+REF_PATH = os.path.join(HERE, "_ref", "librac_ref.so")
+
+_fp = C.POINTER(C.c_float)
+
+
+class Vec2(C.Structure):
+    _fields_ = [("x", C.c_float), ("y", C.c_float)]
+
+
+def build() -> None:
+    """Compile liborc.so (and _ref when the reference sources exist)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _p(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+_orc = None
+_ref = None
+
+
+def orc() -> C.CDLL:
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORC_PATH):
+            build()
+        lib = C.CDLL(ORC_PATH)
+        L, I, F = C.c_long, C.c_int, C.c_float
+        lib.orc_rotate_batch.argtypes = [_fp, _fp, _fp, L, I, I]
+        lib.orc_project_batch.argtypes = [_fp, _fp, _fp, L, I]
+        lib.orc_project_n.argtypes = [F, F, F, I]
+        lib.orc_project_n.restype = F
+        lib.orc_sincos.argtypes = [F, _fp, _fp]
+        lib.orc_rope_cache.argtypes = [_fp, _fp, I, I, F]
+        lib.orc_rope_apply.argtypes = [_fp, _fp, _fp, I, I, I, I]
+        lib.orc_softmax_batch.argtypes = [_fp, _fp, L, I]
+        lib.orc_rmsnorm.argtypes = [_fp, _fp, _fp, F, L, I]
+        lib.orc_layernorm.argtypes = [_fp, _fp, _fp, _fp, F, L, I]
+        lib.orc_exp_batch.argtypes = [_fp, _fp, L]
+        lib.orc_tanh_batch.argtypes = [_fp, _fp, L]
+        lib.orc_rsqrt.argtypes = [F]
+        lib.orc_rsqrt.restype = F
+        lib.orc_gemm.argtypes = [_fp, _fp, _fp, I, I, I, I, I, I, L, L]
+        lib.orc_gemm_composed.argtypes = [_fp, _fp, _fp, I, I, I, I, L, L]
+        lib.orc_gemm_composed_with.argtypes = [C.c_void_p, _fp, _fp, _fp, I, I, I, I, L, L]
+        lib.orc_num_threads.restype = I
+        _orc = lib
+    return _orc
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref() -> C.CDLL:
+    """The reference lib/c (loaded RTLD_LOCAL: its rac_* names stay private)."""
+    global _ref
+    if _ref is None:
+        lib = C.CDLL(REF_PATH, mode=os.RTLD_LOCAL | os.RTLD_NOW)
+        I, F = C.c_int, C.c_float
+        lib.rac_rotate.argtypes = [Vec2, F]
+        lib.rac_rotate.restype = Vec2
+        lib.rac_rotate_n.argtypes = [Vec2, F, I]
+        lib.rac_rotate_n.restype = Vec2
+        lib.rac_project_n.argtypes = [Vec2, F, I]
+        lib.rac_project_n.restype = F
+        lib.rac_rotate_batch.argtypes = [_fp, _fp, _fp, I]
+        lib.rac_sincos.argtypes = [F, _fp, _fp]
+        lib.rac_rsqrt.argtypes = [F]
+        lib.rac_rsqrt.restype = F
+        lib.rac_exp.argtypes = [F]
+        lib.rac_exp.restype = F
+        lib.rac_tanh.argtypes = [F]
+        lib.rac_tanh.restype = F
+        lib.rac_softmax_batch.argtypes = [_fp, _fp, I, I]
+        lib.rac_rmsnorm.argtypes = [_fp, _fp, _fp, F, I, I, C.c_void_p]
+        lib.rac_rmsnorm.restype = I
+        lib.rac_layernorm.argtypes = [_fp, _fp, _fp, _fp, F, I, I, C.c_void_p]
+        lib.rac_layernorm.restype = I
+        lib.rac_rope_cache.argtypes = [_fp, _fp, I, I, F]
+        lib.rac_rope_cache.restype = I
+        lib.rac_rope_apply.argtypes = [_fp, _fp, _fp, I, I, I, I, C.c_void_p]
+        lib.rac_rope_apply.restype = I
+        lib.rac_hal_sgemm.argtypes = [_fp, _fp, _fp, I, I, I, F, F]
+        lib.rac_hal_sgemm.restype = I
+        lib.rac_sgemm.argtypes = [_fp, _fp, _fp, I, I, I, F, F, C.c_void_p]
+        lib.rac_sgemm.restype = I
+        lib.rac_alu_rotate_batch.argtypes = [_fp, _fp, _fp, I]
+        _ref = lib
+    return _ref
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ── numpy front-ends of the restatement ────────────────────────────────────
+
+def rotate_batch(v, theta, iters: int = 16, literal_kinv: bool = True):
+    """v: [n, 2] float32; returns [n, 2]. literal_kinv -> rac_rotate_batch."""
+    v, theta = _f32(v), _f32(theta)
+    out = np.empty_like(v)
+    orc().orc_rotate_batch(_p(v), _p(theta), _p(out), theta.size, iters, int(literal_kinv))
+    return out
+
+
+def project_batch(v, theta, iters: int = 16):
+    v, theta = _f32(v), _f32(theta)
+    out = np.empty_like(theta)
+    orc().orc_project_batch(_p(v), _p(theta), _p(out), theta.size, iters)
+    return out
+
+
+def rope_cache(max_seq: int, head_dim: int, base: float = 10000.0):
+    c = np.empty((max_seq, head_dim // 2), np.float32)
+    s = np.empty_like(c)
+    orc().orc_rope_cache(_p(c), _p(s), max_seq, head_dim, base)
+    return c, s
+
+
+def rope_apply(x, cos_tab, sin_tab):
+    x = _f32(x).copy()
+    b, h, s, hd = x.shape
+    orc().orc_rope_apply(_p(x), _p(_f32(cos_tab)), _p(_f32(sin_tab)), b, h, s, hd)
+    return x
+
+
+def softmax(x):
+    x = _f32(x)
+    out = np.empty_like(x)
+    orc().orc_softmax_batch(_p(x), _p(out), x.size // x.shape[-1], x.shape[-1])
+    return out
+
+
+def rmsnorm(x, gamma=None, eps: float = 1e-6):
+    x = _f32(x)
+    y = np.empty_like(x)
+    g = _p(_f32(gamma)) if gamma is not None else None
+    orc().orc_rmsnorm(_p(x), _p(y), g, eps, x.size // x.shape[-1], x.shape[-1])
+    return y
+
+
+def layernorm(x, gamma=None, beta=None, eps: float = 1e-6):
+    x = _f32(x)
+    y = np.empty_like(x)
+    g = _p(_f32(gamma)) if gamma is not None else None
+    b = _p(_f32(beta)) if beta is not None else None
+    orc().orc_layernorm(_p(x), _p(y), g, b, eps, x.size // x.shape[-1], x.shape[-1])
+    return y
+
+
+def exp(x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    orc().orc_exp_batch(_p(x), _p(y), x.size)
+    return y
+
+
+def tanh(x):
+    x = _f32(x)
+    y = np.empty_like(x)
+    orc().orc_tanh_batch(_p(x), _p(y), x.size)
+    return y
+
+
+LAYOUTS = {"nn": 0, "nt": 1, "tn": 2}
+
+
+def gemm(A, B, layout: str = "nn", mode: int = 1, iters: int = 16, rows=None):
+    """Sequential-k GEMM of rac_kernels.hip (mode 0 FAST, 1 CORDIC).
+
+    Shapes: nn A[M,K] B[K,N]; nt A[M,K] B[N,K]; tn A[K,M] B[K,N].
+    rows=(r0, r1) computes only output rows [r0, r1)."""
+    A, B = _f32(A), _f32(B)
+    lay = LAYOUTS[layout]
+    if lay == 2:
+        K, M = A.shape
+    else:
+        M, K = A.shape
+    N = B.shape[0] if lay == 1 else B.shape[1]
+    r0, r1 = rows if rows is not None else (0, M)
+    C_ = np.empty((r1 - r0, N), np.float32)
+    orc().orc_gemm(_p(A), _p(B), _p(C_), M, N, K, lay, mode, iters, r0, r1)
+    return C_
+
+
+def gemm_composed(A, B, iters: int = 16, rows=None):
+    """CORDIC GEMM composed from rac_project_n, double accumulation (NN)."""
+    A, B = _f32(A), _f32(B)
+    M, K = A.shape
+    N = B.shape[1]
+    r0, r1 = rows if rows is not None else (0, M)
+    C_ = np.empty((r1 - r0, N), np.float32)
+    orc().orc_gemm_composed(_p(A), _p(B), _p(C_), M, N, K, iters, r0, r1)
+    return C_
+
+
+def gemm_composed_ref(A, B, iters: int = 16, rows=None):
+    """CORDIC GEMM composed from the REFERENCE library's rac_project_n."""
+    A, B = _f32(A), _f32(B)
+    M, K = A.shape
+    N = B.shape[1]
+    r0, r1 = rows if rows is not None else (0, M)
+    C_ = np.empty((r1 - r0, N), np.float32)
+    fn = C.cast(ref().rac_project_n, C.c_void_p)
+    orc().orc_gemm_composed_with(fn, _p(A), _p(B), _p(C_), M, N, K, iters, r0, r1)
+    return C_
+
+
+# ── reference-library front-ends ───────────────────────────────────────────
+
+def ref_rotate_batch(v, theta):
+    v, theta = _f32(v), _f32(theta)
+    out = np.empty_like(v)
+    ref().rac_rotate_batch(_p(v), _p(theta), _p(out), theta.size)
+    return out
+
+
+def ref_rotate_n_batch(v, theta, iters):
+    v, theta = _f32(v), _f32(theta)
+    out = np.empty_like(v)
+    f = ref().rac_rotate_n
+    for i in range(theta.size):
+        r = f(Vec2(v[i, 0], v[i, 1]), float(theta[i]), iters)
+        out[i] = (r.x, r.y)
+    return out
+
+
+def ref_project_n_batch(v, theta, iters):
+    v, theta = _f32(v), _f32(theta)
+    f = ref().rac_project_n
+    return np.array([f(Vec2(v[i, 0], v[i, 1]), float(theta[i]), iters)
+                     for i in range(theta.size)], np.float32)
+
+
+def ref_rope_cache(max_seq, head_dim, base=10000.0):
+    c = np.empty((max_seq, head_dim // 2), np.float32)
+    s = np.empty_like(c)
+    assert ref().rac_rope_cache(_p(c), _p(s), max_seq, head_dim, base) == 0
+    return c, s
+
+
+def ref_rope_apply(x, cos_tab, sin_tab):
+    x = _f32(x).copy()
+    b, h, s, hd = x.shape
+    assert ref().rac_rope_apply(_p(x), _p(_f32(cos_tab)), _p(_f32(sin_tab)), b, h, s, hd, None) == 0
+    return x
+
+
+def ref_softmax(x):
+    x = _f32(x)
+    out = np.empty_like(x)
+    ref().rac_softmax_batch(_p(x), _p(out), x.size // x.shape[-1], x.shape[-1])
+    return out
+
+
+def ref_rmsnorm(x, gamma=None, eps=1e-6):
+    x = _f32(x)
+    y = np.empty_like(x)
+    g = _p(_f32(gamma)) if gamma is not None else None
+    assert ref().rac_rmsnorm(_p(x), _p(y), g, eps, x.size // x.shape[-1], x.shape[-1], None) == 0
+    return y
+
+
+def ref_layernorm(x, gamma=None, beta=None, eps=1e-6):
+    x = _f32(x)
+    y = np.empty_like(x)
+    g = _p(_f32(gamma)) if gamma is not None else None
+    b = _p(_f32(beta)) if beta is not None else None
+    assert ref().rac_layernorm(_p(x), _p(y), g, b, eps, x.size // x.shape[-1], x.shape[-1], None) == 0
+    return y
+
+
+def ref_sgemm(A, B):
+    """lib/c HAL SGEMM (AVX2 path): the reference's CPU rac_matmul."""
+    A, B = _f32(A), _f32(B)
+    M, K = A.shape
+    N = B.shape[1]
+    C_ = np.empty((M, N), np.float32)
+    assert ref().rac_hal_sgemm(_p(A), _p(B), _p(C_), M, N, K, 1.0, 0.0) == 0
+    return C_
+
+
+# ── tolerance helpers shared by the tests ──────────────────────────────────
+
+def ulp_distance(a, b) -> np.ndarray:
+    """Distance in units of float32 ordering (0 = bit equal)."""
+    a = _f32(a).view(np.int32).astype(np.int64)
+    b = _f32(b).view(np.int32).astype(np.int64)
+    a = np.where(a < 0, np.int64(-2**31) - a, a)
+    b = np.where(b < 0, np.int64(-2**31) - b, b)
+    return np.abs(a - b)
+
+
+def elementwise_ok(got, want, scale=None, max_ulp: int = 2) -> np.ndarray:
+    """Elementwise bar: <= max_ulp ulps, or |diff| <= max_ulp * ulp(max(1, |scale|))."""
+    got, want = _f32(got), _f32(want)
+    if scale is None:
+        scale = np.maximum(np.abs(want), 1.0)
+    floor = max_ulp * np.spacing(np.maximum(np.abs(_f32(scale)), np.float32(1.0)))
+    return (ulp_distance(got, want) <= max_ulp) | (np.abs(got - want) <= floor)
+
+
+def max_rel_err(got, want) -> float:
+    """Reduction bar metric: max |got-want| / max(|want|, 1e-3 * rms(want))."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    if want.size == 0:
+        return 0.0
+    rms = np.sqrt(np.mean(want * want)) if want.size else 0.0
+    den = np.maximum(np.abs(want), 1e-3 * rms + 1e-30)
+    return float(np.max(np.abs(got - want) / den))

@@ -1,0 +1,6 @@
+// CORDIC GEMM, n = 24 iterations unrolled: NN and NT layouts, vector loads.
+#include "gemm_kernel.cuh"
+namespace racb {
+RACB_GEMM_INST(kCordic, 24, kNN, 1, true) RACB_GEMM_INST(kCordic, 24, kNT, 1, true)
+RACB_GEMM_INST(kCordic, 24, kNN, 3, true) RACB_GEMM_INST(kCordic, 24, kNT, 3, true)
+}

@@ -1,0 +1,7 @@
+// FAST-mode (sign-XOR FMA) GEMM instantiations.
+#include "gemm_kernel.cuh"
+namespace racb {
+#define L(LAY) RACB_GEMM_INST(kFast, 0, LAY, 1, true) RACB_GEMM_INST(kFast, 0, LAY, 1, false) \
+               RACB_GEMM_INST(kFast, 0, LAY, 3, true) RACB_GEMM_INST(kFast, 0, LAY, 3, false)
+L(kNN) L(kNT) L(kTN)
+}

@@ -1,0 +1,239 @@
+// gemm_kernel.cuh -- the rotation-accumulate GEMM for sm_100a.
+//
+// C[M,N] = alpha * sum_k MAC(A[m,k], B[k,n]) (+ beta*Cin) (+ bias) -> act,
+// where MAC is one of the reference's per-element products
+// (rac_torch/rac_kernels.hip:203-219):
+//   FAST   -- sign-XOR FMA (rac_kernels.hip:56-64).  (a ^ sign b) * |b| is
+//             bit-identical to a * b, so it is issued as one FFMA.
+//   CORDIC -- rac_fma_cordic (rac_kernels.hip:176-185): (a, 0) rotated by
+//             angle(b) in {0, pi} through `iters` micro-rotations, x scaled
+//             by 1/K(iters), accumulated as fmaf(x * k_inv, |b|, acc).
+//
+// The CORDIC MAC costs 2*iters FP32/INT instructions (1 LOP3 for the fold,
+// 2*iters-3 FFMA for iterations 1..iters-1 -- iteration 0 is an exact copy --
+// 1 FMUL, 1 FFMA), so the kernel is bound by the SM's FP32 issue rate, not
+// by memory: a 64x128 tile with K=4096 moves 3 MB from L2 for ~5e9 issued
+// instructions.  The design therefore spends its effort on issue efficiency:
+// an 8x8 register tile per thread gives 64 independent rotation chains for
+// the scheduler to interleave, operands are staged through shared memory
+// with a register double buffer so loads never sit on the issue path, and
+// each output accumulates sequentially over k (the reference kernels'
+// order), which keeps the result bit-identical to the CPU restatement.
+// No tensor cores: the defining arithmetic is the micro-rotation, not a MAC.
+#pragma once
+#include "rac_device.cuh"
+#include "rac_internal.h"
+
+namespace racb {
+
+__device__ __forceinline__ float apply_act(float x, int act) {
+    // rac_torch/rac_torch.cu:668-676 (_apply_act).
+    switch (act) {
+        case kActRelu: return x > 0.0f ? x : 0.0f;
+        case kActGelu: return x * 0.5f * (1.0f + erff(x * 0.7071067811865f));
+        case kActSilu: return __fdiv_rn(x, 1.0f + expf(-x));
+        default: return x;
+    }
+}
+
+// Global -> register -> shared staging of one operand tile.
+//   ROWS x COLS tile of a row-major matrix (COLS contiguous, leading dim ld),
+//   stored into smem as S[k][mn] with k along COLS (TRANS) or along ROWS.
+template <int ROWS, int COLS, int NT, bool VEC>
+struct TileLoader {
+    static constexpr int ELEMS = ROWS * COLS;
+    static constexpr int PER = VEC ? 4 : 1;
+    static constexpr int LOADS = (ELEMS + PER * NT - 1) / (PER * NT);
+    static constexpr bool PARTIAL = (ELEMS % (PER * NT)) != 0;
+    static_assert(!PARTIAL || LOADS == 1, "partial tiles only when a tile needs one pass");
+    float r[LOADS * PER];
+
+    __device__ __forceinline__ void load(const float* __restrict__ src, long long ld,
+                                         int row0, int col0, int rows_lim, int cols_lim,
+                                         int tid) {
+#pragma unroll
+        for (int l = 0; l < LOADS; ++l) {
+            const int idx = (tid + l * NT) * PER;
+            if (PARTIAL && idx >= ELEMS) break;
+            const int rr = idx / COLS, cc = idx % COLS;
+            const int gr = row0 + rr, gc = col0 + cc;
+            if constexpr (VEC) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                // cols_lim is a multiple of 4 on the VEC path, so a vector is
+                // either fully inside or fully outside.
+                if (gr < rows_lim && gc < cols_lim)
+                    v = __ldg(reinterpret_cast<const float4*>(src + (long long)gr * ld + gc));
+                r[l * 4 + 0] = v.x; r[l * 4 + 1] = v.y;
+                r[l * 4 + 2] = v.z; r[l * 4 + 3] = v.w;
+            } else {
+                r[l] = (gr < rows_lim && gc < cols_lim) ? __ldg(src + (long long)gr * ld + gc) : 0.0f;
+            }
+        }
+    }
+
+    // K_ALONG_COLS: the tile's columns are k (store transposed: S[c][r]);
+    // otherwise the tile's rows are k (S[r][c]).  S has row length SLD.
+    template <bool K_ALONG_COLS, int SLD>
+    __device__ __forceinline__ void store(float* S, int tid) const {
+#pragma unroll
+        for (int l = 0; l < LOADS; ++l) {
+            const int idx = (tid + l * NT) * PER;
+            if (PARTIAL && idx >= ELEMS) break;
+            const int rr = idx / COLS, cc = idx % COLS;
+            if constexpr (K_ALONG_COLS) {
+#pragma unroll
+                for (int q = 0; q < PER; ++q) S[(cc + q) * SLD + rr] = r[l * PER + q];
+            } else {
+                if constexpr (VEC) {
+                    *reinterpret_cast<float4*>(&S[rr * SLD + cc]) =
+                        make_float4(r[l * 4 + 0], r[l * 4 + 1], r[l * 4 + 2], r[l * 4 + 3]);
+                } else {
+                    S[rr * SLD + cc] = r[l];
+                }
+            }
+        }
+    }
+};
+
+template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+k_gemm(const __grid_constant__ GemmParams p) {
+    constexpr int TX = BN / TN, TY = BM / TM, NT = TX * TY;
+    // Tiles are k-major in shared memory: row kk holds BM (BN) operands.
+    __shared__ __align__(16) float As[2][BK * BM];
+    __shared__ __align__(16) float Bs[2][BK * BN];
+
+    const int tid = threadIdx.x;
+    const int tx = tid % TX, ty = tid / TX;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+
+    // A: NN/NT store A[M,K] (k contiguous); TN stores A[K,M].
+    // B: NN/TN store B[K,N] (n contiguous); NT stores B[N,K].
+    constexpr bool A_KCOLS = (LAYOUT != kTN);
+    constexpr bool B_KCOLS = (LAYOUT == kNT);
+    TileLoader<A_KCOLS ? BM : BK, A_KCOLS ? BK : BM, NT, VEC> la;
+    TileLoader<B_KCOLS ? BN : BK, B_KCOLS ? BK : BN, NT, VEC> lb;
+
+    auto load_tiles = [&](int k0) {
+        if constexpr (A_KCOLS) la.load(p.A, p.lda, m0, k0, p.M, p.K, tid);
+        else                   la.load(p.A, p.lda, k0, m0, p.K, p.M, tid);
+        if constexpr (B_KCOLS) lb.load(p.B, p.ldb, n0, k0, p.N, p.K, tid);
+        else                   lb.load(p.B, p.ldb, k0, n0, p.K, p.N, tid);
+    };
+    auto store_tiles = [&](int buf) {
+        la.template store<A_KCOLS, BM>(As[buf], tid);
+        lb.template store<B_KCOLS, BN>(Bs[buf], tid);
+    };
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+
+    const float k_inv = p.k_inv;
+    const int ktiles = (p.K + BK - 1) / BK;
+
+    load_tiles(0);
+    store_tiles(0);
+    __syncthreads();
+
+    for (int kt = 0; kt < ktiles; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < ktiles) load_tiles((kt + 1) * BK);   // in flight during compute
+
+        const float* __restrict__ Asb = As[buf];
+        const float* __restrict__ Bsb = Bs[buf];
+#pragma unroll 1
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[TM], b[TN];
+#pragma unroll
+            for (int i = 0; i < TM; i += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(&Asb[kk * BM + ty * TM + i]);
+                a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
+            }
+#pragma unroll
+            for (int j = 0; j < TN; j += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(&Bsb[kk * BN + tx * TN + j]);
+                b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+            }
+            if constexpr (MODE == kFast) {
+#pragma unroll
+                for (int i = 0; i < TM; ++i)
+#pragma unroll
+                    for (int j = 0; j < TN; ++j)
+                        acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+            } else {
+                uint32_t sgn[TN];
+                float mag[TN];
+#pragma unroll
+                for (int j = 0; j < TN; ++j) {
+                    sgn[j] = __float_as_uint(b[j]) & 0x80000000u;
+                    mag[j] = __uint_as_float(__float_as_uint(b[j]) & 0x7FFFFFFFu);
+                }
+#pragma unroll
+                for (int j = 0; j < TN; ++j) {
+#pragma unroll
+                    for (int i = 0; i < TM; ++i) {
+                        const float sa = __uint_as_float(__float_as_uint(a[i]) ^ sgn[j]);
+                        float x;
+                        if constexpr (ITERS > 0) x = gemm_cordic_x<ITERS>(sa);
+                        else                     x = gemm_cordic_x_rt(sa, p.iters, p.coef);
+                        acc[i][j] = __fmaf_rn(__fmul_rn(x, k_inv), mag[j], acc[i][j]);
+                    }
+                }
+            }
+        }
+        if (kt + 1 < ktiles) {
+            store_tiles(buf ^ 1);
+        }
+        __syncthreads();
+    }
+
+    // Epilogue (rac_kernels.hip:790-797 for alpha/beta; rac_torch.cu:769-776
+    // for bias + activation).
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int gm = m0 + ty * TM + i;
+        if (gm >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            const int gn = n0 + tx * TN + j;
+            if (gn >= p.N) continue;
+            float v;
+            if (p.beta != 0.0f)
+                v = __fmaf_rn(p.alpha, acc[i][j], __fmul_rn(p.beta, p.Cin[(long long)gm * p.ldcin + gn]));
+            else
+                v = __fmul_rn(p.alpha, acc[i][j]);
+            if (p.bias) v = __fadd_rn(v, p.bias[gn]);
+            if (p.act) v = apply_act(v, p.act);
+            p.C[(long long)gm * p.ldc + gn] = v;
+        }
+    }
+}
+
+// Tile variants.  1: 64x128 CTA tile, 8x8 per thread (the general case);
+// 3: 16x128, 4x4 per thread (M <= 32, e.g. decode-shaped rows).
+template <int V> struct TileCfg;
+template <> struct TileCfg<1> { static constexpr int BM = 64, BN = 128, BK = 8, TM = 8, TN = 8; };
+template <> struct TileCfg<2> { static constexpr int BM = 64, BN = 64, BK = 8, TM = 8, TN = 4; };
+template <> struct TileCfg<3> { static constexpr int BM = 16, BN = 128, BK = 8, TM = 4, TN = 4; };
+
+template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
+int launch_inst(const GemmParams& p, cudaStream_t s) {
+    using T = TileCfg<V>;
+    constexpr int NT = (T::BM / T::TM) * (T::BN / T::TN);
+    dim3 grid((p.N + T::BN - 1) / T::BN, (p.M + T::BM - 1) / T::BM);
+    if (grid.y > 65535) return kErrInvalidDim;
+    k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC><<<grid, NT, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+// Explicit instantiations live in gemm_inst_*.cu so that the heavy unrolled
+// kernels compile in parallel translation units.
+#define RACB_GEMM_INST(MODE, ITERS, LAYOUT, V, VEC) \
+    template int launch_inst<MODE, ITERS, LAYOUT, V, VEC>(const GemmParams&, cudaStream_t);
+#define RACB_GEMM_EXTERN(MODE, ITERS, LAYOUT, V, VEC) \
+    extern template int launch_inst<MODE, ITERS, LAYOUT, V, VEC>(const GemmParams&, cudaStream_t);
+
+}  // namespace racb

@@ -1,0 +1,208 @@
+// rac_device.cuh -- device-side CORDIC primitives for sm_100a.
+//
+// Semantics follow the reference CPU library lib/c/rac_cpu.c (the parity
+// target) and the GPU GEMM of rac_torch/rac_kernels.hip; every rounding step
+// is written with an explicit __f*_rn intrinsic so that nvcc cannot contract
+// or reassociate it.  Cited lines are inside the Pinnacle-Quantum-Group/RAC
+// project.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace racb {
+
+// RAC_PI, RAC_K_INV, RAC_ITERS: lib/c/rac_cpu.h:39-42.
+constexpr float kPi = 3.14159265358979f;
+constexpr float kKInv = 0.60725f;
+constexpr int kDefaultIters = 16;
+constexpr int kMaxIters = 24;
+// Upper bound on the (-pi, pi] wrap loop of _cordic_rotate (lib/c/rac_cpu.c:93-94).
+// The reference loops forever when theta - 2*pi == theta (|theta| >= 2^25 or
+// inf); a GPU thread must not, so the loop stops here and flags the launch.
+constexpr int kWrapLimit = 1 << 20;
+
+// atan(2^-i) table, i = 0..23 (lib/c/rac_cpu.c:20-25 + :37-40; identical in
+// rac_torch/rac_kernels.hip:32-39), for runtime-indexed loops.
+__device__ __constant__ static const float kAtanTab[24] = {
+    0.78539816f, 0.46364761f, 0.24497866f, 0.12435499f,
+    0.06241881f, 0.03123983f, 0.01562373f, 0.00781234f,
+    0.00390623f, 0.00195312f, 0.00097656f, 0.00048828f,
+    0.00024414f, 0.00012207f, 0.00006104f, 0.00003052f,
+    0.00001526f, 0.00000763f, 0.00000381f, 0.00000191f,
+    0.00000095f, 0.00000048f, 0.00000024f, 0.00000012f,
+};
+
+// The same table as a constexpr function, so that unrolled device loops fold
+// table entries to immediates (the __constant__ copy serves runtime indices).
+__host__ __device__ constexpr float atan_entry(int i) {
+    constexpr float t[24] = {
+        0.78539816f, 0.46364761f, 0.24497866f, 0.12435499f,
+        0.06241881f, 0.03123983f, 0.01562373f, 0.00781234f,
+        0.00390623f, 0.00195312f, 0.00097656f, 0.00048828f,
+        0.00024414f, 0.00012207f, 0.00006104f, 0.00003052f,
+        0.00001526f, 0.00000763f, 0.00000381f, 0.00000191f,
+        0.00000095f, 0.00000048f, 0.00000024f, 0.00000012f,
+    };
+    return t[i];
+}
+
+// CORDIC gain K(n), n = 0..24 (lib/c/rac_cpu.c:44-52, rac_kernels.hip:42-50).
+__host__ __device__ constexpr float k_entry(int n) {
+    constexpr float t[25] = {
+        1.00000000f, 1.41421356f, 1.58113883f, 1.62979295f,
+        1.64248460f, 1.64568447f, 1.64648404f, 1.64668388f,
+        1.64673383f, 1.64674632f, 1.64674944f, 1.64675022f,
+        1.64675042f, 1.64675047f, 1.64675048f, 1.64675049f,
+        1.64675049f, 1.64675049f, 1.64675049f, 1.64675049f,
+        1.64675049f, 1.64675049f, 1.64675049f, 1.64675049f,
+        1.64675049f,
+    };
+    return t[n];
+}
+
+// Direction sequence of the GEMM MAC.  In rac_fma_cordic
+// (rac_kernels.hip:176-185) b is encoded as angle 0 or pi; pi folds to 0 with
+// a negated vector (:144-150), so the residual angle always starts at +0 and
+// d_i = sign(angle_i) follows from the atan table alone:
+//   angle_0 = 0, d_i = (angle_i >= 0) ? +1 : -1, angle_{i+1} = angle_i - d_i*atan_i
+// evaluated in float32.  A host test recomputes the recursion and checks it
+// against rac_b200_cordic_gemm_directions() (exported by the shim).
+__host__ __device__ constexpr int gemm_dir(int i) {
+    constexpr int t[24] = {
+        +1, -1, -1, -1, +1, -1, +1, +1, -1, -1, -1, -1,
+        +1, +1, -1, -1, +1, +1, -1, -1, +1, -1, -1, +1,
+    };
+    return t[i];
+}
+
+// 2^-i (exact).
+__host__ __device__ constexpr float pow2neg(int i) {
+    float s = 1.0f;
+    for (int t = 0; t < i; ++t) s *= 0.5f;
+    return s;
+}
+
+// d_i * 2^-i, the micro-rotation coefficient of iteration i of the GEMM MAC.
+__host__ __device__ constexpr float gemm_coef(int i) {
+    return gemm_dir(i) > 0 ? pow2neg(i) : -pow2neg(i);
+}
+
+// One CORDIC MAC of rac_fma_cordic (rac_kernels.hip:176-185) with the fold
+// already applied: the vector entering the iterations is (sa, 0) where
+// sa = a with b's sign bit xor-ed in (the fold negates it when b < 0).
+// Iteration 0 has scale 1 and y = 0, so it maps (sa, 0) to (sa, sa) exactly;
+// iterations 1..ITERS-1 are x' = x - c_i*y, y' = y + c_i*x with c_i = d_i*2^-i
+// (one rounding each: c_i*y is exact).  Only x of the last iteration is used.
+// Returns x_n (before the 1/K(n) compensation).
+template <int ITERS>
+__device__ __forceinline__ float gemm_cordic_x(float sa) {
+    float x = sa, y = sa;
+#pragma unroll
+    for (int t = 1; t < ITERS; ++t) {
+        const float c = gemm_coef(t);
+        if (t == ITERS - 1) {
+            x = __fmaf_rn(-c, y, x);
+        } else {
+            const float xn = __fmaf_rn(-c, y, x);
+            y = __fmaf_rn(c, x, y);
+            x = xn;
+        }
+    }
+    return x;
+}
+
+// Runtime-iteration variant (any n in [1, 24]); coefficients come from a
+// kernel-argument table.
+__device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
+                                                   const float* coef) {
+    float x = sa, y = sa;
+    for (int t = 1; t < iters; ++t) {
+        const float c = coef[t];
+        const float xn = __fmaf_rn(-c, y, x);
+        y = __fmaf_rn(c, x, y);
+        x = xn;
+    }
+    return x;
+}
+
+// _cordic_rotate of lib/c/rac_cpu.c:90-118: wrap theta to (-pi, pi], fold
+// into [-pi/2, pi/2] by negating (x, y), then ITERS micro-rotations whose
+// direction is the sign of the residual angle.  (x, y) arrive pre-scaled.
+// The direction is read from the angle's sign bit: the residual can only be
+// -0 at entry (x - y == 0 rounds to +0 afterwards), which the +0.0f add
+// removes, and a NaN angle takes the comparison path to keep d = -1.
+// Returns false when the wrap loop hit kWrapLimit.
+template <int ITERS>
+__device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta) {
+    const float TAU = 2.0f * kPi;
+    bool ok = true;
+    int w = 0;
+    while (theta > kPi) { theta = __fsub_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+    while (theta <= -kPi) { theta = __fadd_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+    float x = xr, y = yr;
+    if (theta > kPi * 0.5f) {
+        x = -x; y = -y; theta = __fsub_rn(theta, kPi);
+    } else if (theta < -kPi * 0.5f) {
+        x = -x; y = -y; theta = __fadd_rn(theta, kPi);
+    }
+    if (theta != theta) {
+        // NaN residual: every comparison is false, so d = -1 throughout.
+        float s = 1.0f;
+#pragma unroll
+        for (int i = 0; i < ITERS; ++i) {
+            const float xn = __fmaf_rn(s, y, x);
+            y = __fmaf_rn(-s, x, y);
+            x = xn;
+            s *= 0.5f;
+        }
+    } else {
+        float angle = __fadd_rn(theta, 0.0f);   // -0 -> +0
+#pragma unroll
+        for (int i = 0; i < ITERS; ++i) {
+            const uint32_t sgn = __float_as_uint(angle) & 0x80000000u;
+            const float ds = __uint_as_float(__float_as_uint(pow2neg(i)) ^ sgn);
+            const float xn = __fmaf_rn(-ds, y, x);
+            y = __fmaf_rn(ds, x, y);
+            x = xn;
+            if (i + 1 < ITERS)
+                angle = __fsub_rn(angle, __uint_as_float(__float_as_uint(atan_entry(i)) ^ sgn));
+        }
+    }
+    xr = x; yr = y;
+    return ok;
+}
+
+// Runtime-iteration version of the same rotation (iters in [1, 24]).
+__device__ __forceinline__ bool cordic_rotate_rt(float& xr, float& yr, float theta, int iters) {
+    const float TAU = 2.0f * kPi;
+    bool ok = true;
+    int w = 0;
+    while (theta > kPi) { theta = __fsub_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+    while (theta <= -kPi) { theta = __fadd_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+    float x = xr, y = yr;
+    if (theta > kPi * 0.5f) {
+        x = -x; y = -y; theta = __fsub_rn(theta, kPi);
+    } else if (theta < -kPi * 0.5f) {
+        x = -x; y = -y; theta = __fadd_rn(theta, kPi);
+    }
+    float angle = theta, s = 1.0f;
+    for (int i = 0; i < iters; ++i) {
+        const float d = (angle >= 0.0f) ? 1.0f : -1.0f;
+        const float ds = d * s;                     // exact
+        const float xn = __fmaf_rn(-ds, y, x);
+        y = __fmaf_rn(ds, x, y);
+        x = xn;
+        angle = __fsub_rn(angle, d * kAtanTab[i]);  // d * atan is exact
+        s *= 0.5f;
+    }
+    xr = x; yr = y;
+    return ok;
+}
+
+// 1/K(n) in float, as both reference libraries compute it at run time
+// (lib/c/rac_cpu.c:277, rac_kernels.hip:182).
+__host__ __device__ inline float k_inv_of(int iters) {
+    return 1.0f / k_entry(iters);
+}
+
+}  // namespace racb

@@ -1,0 +1,50 @@
+// rac_internal.h -- declarations shared by the .cu files of librac_b200.so.
+// Nothing here is part of the public C ABI (that is include/rac.h and
+// include/rac_b200.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace racb {
+
+enum Layout : int { kNN = 0, kNT = 1, kTN = 2 };
+enum Mode : int { kFast = 0, kCordic = 1, kShiftAdd = 2 };
+enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActSilu = 3 };
+
+// Status codes: lib/c/rac_cpu.h:54-59 plus the GPU-side ones.
+enum Status : int {
+    kOk = 0,
+    kErrNullPtr = -1,
+    kErrInvalidDim = -2,
+    kErrAlloc = -3,
+    kErrCuda = -4,
+    kErrUnsupported = -5,
+    kErrDevice = -6,      // a kernel reported a bounded-loop overrun
+    kErrNoScratch = -7,
+};
+
+struct GemmParams {
+    const float* A;
+    const float* B;
+    float* C;
+    const float* Cin;     // read when beta != 0 (may alias C)
+    const float* bias;    // [N] or nullptr
+    int M, N, K;
+    long long lda, ldb, ldc, ldcin;
+    float alpha, beta;
+    int act;
+    int iters;            // CORDIC iteration count (runtime-iteration kernels)
+    float k_inv;          // 1/K(iters)
+    float coef[24];       // d_i * 2^-i (runtime-iteration kernels)
+};
+
+// Launches one GEMM on `stream`. variant 0 = automatic tile choice; the other
+// values select a fixed tile (used by the tile sweep in the benchmark).
+// Returns a Status; never synchronises.
+int launch_gemm(const GemmParams& p, int layout, int mode, int variant,
+                cudaStream_t stream);
+
+// Per-device error word that bounded device loops set (see rac_device.cuh).
+unsigned int* device_error_word(int device);
+
+}  // namespace racb

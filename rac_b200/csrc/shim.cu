@@ -1,0 +1,576 @@
+// shim.cu -- the C ABI of librac_b200.so (include/rac.h, include/rac_b200.h).
+//
+// Blocking rac.h entry points accept host or device pointers: device (or
+// managed) memory is used in place; host memory is staged through
+// stream-ordered device allocations on a per-thread, per-device stream.
+// Every call records a thread-local status (rac_last_error) and never
+// aborts.  There is no CPU path: without a device the call fails with
+// RAC_ERR_CUDA.
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "rac_device.cuh"
+#include "rac_internal.h"
+#include "stream_ops.h"
+#include "rac_b200.h"
+
+#define RAC_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+using namespace racb;
+
+thread_local int t_status = 0;
+thread_local char t_msg[256] = "ok";
+
+int set_status(int st, const char* what) {
+    t_status = st;
+    if (st == 0) {
+        std::snprintf(t_msg, sizeof t_msg, "ok");
+    } else {
+        const char* kind = st == kErrNullPtr ? "null pointer" : st == kErrInvalidDim ? "invalid dimension"
+                         : st == kErrAlloc ? "allocation failed" : st == kErrCuda ? "CUDA error"
+                         : st == kErrUnsupported ? "unsupported" : st == kErrDevice ? "device loop limit"
+                         : "error";
+        cudaError_t ce = cudaGetLastError();
+        std::snprintf(t_msg, sizeof t_msg, "%s: %s%s%s", what, kind,
+                      ce != cudaSuccess ? " / " : "", ce != cudaSuccess ? cudaGetErrorString(ce) : "");
+    }
+    return st;
+}
+
+std::atomic<int> g_iters{-1};
+std::atomic<int> g_mode{-1};
+
+int clamp_gemm_iters(int n) { return n < 1 ? 1 : (n > kMaxIters ? kMaxIters : n); }
+
+void init_knobs() {
+    if (g_iters.load() < 0) {
+        int it = kDefaultIters;
+        if (const char* e = std::getenv("RAC_CORDIC_ITERS")) { int v = std::atoi(e); if (v > 0) it = clamp_gemm_iters(v); }
+        int expected = -1;
+        g_iters.compare_exchange_strong(expected, it);
+    }
+    if (g_mode.load() < 0) {
+        int m = kCordic;
+        if (const char* e = std::getenv("RAC_CORDIC_MODE")) {
+            if (!std::strcmp(e, "fast") || !std::strcmp(e, "0")) m = kFast;
+        }
+        int expected = -1;
+        g_mode.compare_exchange_strong(expected, m);
+    }
+}
+
+int device_ready(int* dev_out) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) { cudaGetLastError(); return kErrCuda; }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+    if (dev_out) *dev_out = dev;
+    return kOk;
+}
+
+// Per-thread, per-device stream for blocking calls.
+cudaStream_t call_stream(int dev) {
+    thread_local std::vector<cudaStream_t> streams;
+    if ((int)streams.size() <= dev) streams.resize(dev + 1, nullptr);
+    if (!streams[dev]) cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking);
+    return streams[dev];
+}
+
+bool is_device_ptr(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) { cudaGetLastError(); return false; }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// One staged buffer of a blocking call.
+struct Buf {
+    const void* user = nullptr;
+    void* dev = nullptr;
+    size_t bytes = 0;
+    bool staged = false;
+    bool out = false;
+};
+
+// Scope of a blocking call: stages inputs in, outputs back, frees, syncs.
+struct Call {
+    int dev = 0;
+    cudaStream_t s = nullptr;
+    std::vector<Buf> bufs;
+    int st = kOk;
+
+    int begin() {
+        st = device_ready(&dev);
+        if (st == kOk) s = call_stream(dev);
+        if (st == kOk && !s) st = kErrCuda;
+        return st;
+    }
+    // in: copy host data to the device; out: copy back at finish.
+    void* map(const void* p, size_t bytes, bool in, bool out) {
+        if (st != kOk || !p) return const_cast<void*>(p);
+        if (bytes == 0 || is_device_ptr(p)) return const_cast<void*>(p);
+        Buf b;
+        b.user = p; b.bytes = bytes; b.staged = true; b.out = out;
+        if (cudaMallocAsync(&b.dev, bytes, s) != cudaSuccess) { st = kErrAlloc; return nullptr; }
+        if (in && cudaMemcpyAsync(b.dev, p, bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) st = kErrCuda;
+        bufs.push_back(b);
+        return b.dev;
+    }
+    int finish(int launch_status, bool check_loops) {
+        if (st == kOk) st = launch_status;
+        for (auto& b : bufs) {
+            if (st == kOk && b.out &&
+                cudaMemcpyAsync(const_cast<void*>(b.user), b.dev, b.bytes, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+                st = kErrCuda;
+            cudaFreeAsync(b.dev, s);
+        }
+        if (s && cudaStreamSynchronize(s) != cudaSuccess && st == kOk) st = kErrCuda;
+        if (st == kOk && check_loops) {
+            unsigned int* w = device_error_word(dev);
+            unsigned int h = 0;
+            if (w && cudaMemcpy(&h, w, sizeof h, cudaMemcpyDeviceToHost) == cudaSuccess && h) {
+                cudaMemset(w, 0, sizeof h);
+                st = kErrDevice;
+            }
+        }
+        return st;
+    }
+};
+
+}  // namespace
+
+// ── 1. errors and knobs ─────────────────────────────────────────────────
+
+RAC_API int rac_last_error(void) { return t_status; }
+RAC_API const char* rac_last_error_string(void) { return t_msg; }
+RAC_API void rac_clear_error(void) { set_status(0, ""); }
+
+RAC_API void rac_set_cordic_iters(int iters) {
+    // rac_torch_bind.cpp:205-212: <= 0 resets to the default, else clamp [1, 24].
+    init_knobs();
+    g_iters.store(iters <= 0 ? kDefaultIters : clamp_gemm_iters(iters));
+}
+RAC_API int rac_get_cordic_iters(void) { init_knobs(); return g_iters.load(); }
+RAC_API void rac_set_cordic_mode(int mode) {
+    // rac_torch_bind.cpp:216-219: out-of-range modes fall back to FAST.
+    init_knobs();
+    g_mode.store(mode == kCordic ? kCordic : kFast);
+}
+RAC_API int rac_get_cordic_mode(void) { init_knobs(); return g_mode.load(); }
+
+RAC_API const char* rac_b200_version(void) { return "rac_b200 0.1 (sm_100a)"; }
+RAC_API int rac_b200_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
+}
+RAC_API void rac_b200_cordic_gemm_directions(int out[24]) {
+    if (!out) return;
+    for (int i = 0; i < 24; ++i) out[i] = gemm_dir(i);
+}
+
+// ── 3. stream-ordered device entry points ───────────────────────────────
+
+static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+RAC_API int rac_gemm_async(const float* A, long long lda, const float* B, long long ldb,
+                           float* C, long long ldc, const float* Cin, long long ldcin,
+                           const float* bias, int M, int N, int K, int layout, int mode,
+                           int iters, float alpha, float beta, int act, int variant,
+                           void* stream) {
+    init_knobs();
+    if (iters <= 0) iters = g_iters.load();
+    if (mode < 0) mode = g_mode.load();
+    GemmParams p{};
+    p.A = A; p.B = B; p.C = C; p.Cin = Cin ? Cin : C; p.bias = bias;
+    p.M = M; p.N = N; p.K = K;
+    p.lda = lda; p.ldb = ldb; p.ldc = ldc; p.ldcin = Cin ? ldcin : ldc;
+    p.alpha = alpha; p.beta = beta; p.act = act;
+    p.iters = clamp_gemm_iters(iters);
+    if (act < kActNone || act > kActSilu) return set_status(kErrUnsupported, "rac_gemm_async");
+    if (M == 0 || N == 0) return set_status(kOk, "rac_gemm_async");
+    return set_status(launch_gemm(p, layout, mode, variant, as_stream(stream)), "rac_gemm_async");
+}
+
+static void launch_layout(const float* A, const float* B, float* C, int M, int N, int K,
+                          float alpha, float beta, int iters, int mode, void* stream,
+                          int layout, const char* name) {
+    // Contiguous row-major operands, as in rac_kernels.hip:822-883.
+    const long long lda = layout == kTN ? M : K;
+    const long long ldb = layout == kNT ? K : N;
+    int st = rac_gemm_async(A, lda, B, ldb, C, N, C, N, nullptr, M, N, K, layout, mode, iters,
+                            alpha, beta, kActNone, 0, stream);
+    set_status(st, name);
+}
+
+RAC_API void rac_launch_nn_iters(const float* A, const float* B, float* C, int M, int N, int K,
+                                 float alpha, float beta, int iters, int mode, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, iters, mode, stream, kNN, "rac_launch_nn_iters");
+}
+RAC_API void rac_launch_nt_iters(const float* A, const float* B, float* C, int M, int N, int K,
+                                 float alpha, float beta, int iters, int mode, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, iters, mode, stream, kNT, "rac_launch_nt_iters");
+}
+RAC_API void rac_launch_tn_iters(const float* A, const float* B, float* C, int M, int N, int K,
+                                 float alpha, float beta, int iters, int mode, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, iters, mode, stream, kTN, "rac_launch_tn_iters");
+}
+// rac_kernels.hip:886-909 defaults: iters 24, FAST.
+RAC_API void rac_launch_nn(const float* A, const float* B, float* C, int M, int N, int K,
+                           float alpha, float beta, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, 24, kFast, stream, kNN, "rac_launch_nn");
+}
+RAC_API void rac_launch_nt(const float* A, const float* B, float* C, int M, int N, int K,
+                           float alpha, float beta, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, 24, kFast, stream, kNT, "rac_launch_nt");
+}
+RAC_API void rac_launch_tn(const float* A, const float* B, float* C, int M, int N, int K,
+                           float alpha, float beta, void* stream) {
+    launch_layout(A, B, C, M, N, K, alpha, beta, 24, kFast, stream, kTN, "rac_launch_tn");
+}
+
+RAC_API int rac_rotate_batch_async(const float2* v, const float* theta, float2* out, long long n,
+                                   int iters, int literal_kinv, void* stream) {
+    return set_status(rotate_batch(v, theta, out, n, iters, literal_kinv, as_stream(stream)),
+                      "rac_rotate_batch_async");
+}
+RAC_API int rac_project_batch_async(const float2* v, const float* theta, float* out, long long n,
+                                    int iters, void* stream) {
+    return set_status(project_batch(v, theta, out, n, iters, as_stream(stream)), "rac_project_batch_async");
+}
+RAC_API int rac_sincos_batch_async(const float* theta, float* s, float* c, long long n, void* stream) {
+    return set_status(sincos_batch(theta, s, c, n, as_stream(stream)), "rac_sincos_batch_async");
+}
+RAC_API int rac_unary_async(const float* x, float* y, long long n, int op, void* stream) {
+    return set_status(unary_batch(x, y, n, op, as_stream(stream)), "rac_unary_async");
+}
+RAC_API int rac_softmax_async(const float* x, float* y, long long rows, int d, void* stream) {
+    return set_status(softmax_rows(x, y, rows, d, as_stream(stream)), "rac_softmax_async");
+}
+RAC_API int rac_rmsnorm_async(const float* x, float* y, const float* gamma, float eps,
+                              long long rows, int d, void* stream) {
+    return set_status(rmsnorm_rows(x, y, gamma, eps, rows, d, as_stream(stream)), "rac_rmsnorm_async");
+}
+RAC_API int rac_layernorm_async(const float* x, float* y, const float* gamma, const float* beta,
+                                float eps, long long rows, int d, void* stream) {
+    return set_status(layernorm_rows(x, y, gamma, beta, eps, rows, d, as_stream(stream)),
+                      "rac_layernorm_async");
+}
+RAC_API int rac_rope_cache_async(float* cos_out, float* sin_out, int max_seq, int head_dim,
+                                 float base, void* stream) {
+    return set_status(rope_cache(cos_out, sin_out, max_seq, head_dim, base, as_stream(stream)),
+                      "rac_rope_cache_async");
+}
+RAC_API int rac_rope_apply_async(float* x, const float* cos_tab, const float* sin_tab,
+                                 const int* pos, long long batch_heads, int seq, int head_dim,
+                                 int form, void* stream) {
+    return set_status(rope_apply(x, cos_tab, sin_tab, pos, batch_heads, seq, head_dim, form,
+                                 as_stream(stream)), "rac_rope_apply_async");
+}
+RAC_API int rac_check_device_errors(void* stream) {
+    int dev = 0;
+    int st = device_ready(&dev);
+    if (st != kOk) return set_status(st, "rac_check_device_errors");
+    if (cudaStreamSynchronize(as_stream(stream)) != cudaSuccess)
+        return set_status(kErrCuda, "rac_check_device_errors");
+    unsigned int* w = device_error_word(dev);
+    unsigned int h = 0;
+    if (!w || cudaMemcpy(&h, w, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return set_status(kErrCuda, "rac_check_device_errors");
+    if (h) { cudaMemset(w, 0, sizeof h); return set_status(kErrDevice, "rac_check_device_errors"); }
+    return set_status(kOk, "rac_check_device_errors");
+}
+
+// ── blocking entry points (rac.h and batch forms) ───────────────────────
+
+static int do_matmul(const float* A, const float* B, float* C, int M, int N, int K, int iters,
+                     int mode) {
+    if (!A || !B || !C) return kErrNullPtr;
+    if (M <= 0 || N <= 0 || K <= 0) return kErrInvalidDim;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    const float* dA = (const float*)c.map(A, sizeof(float) * (size_t)M * K, true, false);
+    const float* dB = (const float*)c.map(B, sizeof(float) * (size_t)K * N, true, false);
+    float* dC = (float*)c.map(C, sizeof(float) * (size_t)M * N, false, true);
+    int st = kOk;
+    if (c.st == kOk) {
+        init_knobs();
+        GemmParams p{};
+        p.A = dA; p.B = dB; p.C = dC; p.Cin = dC;
+        p.M = M; p.N = N; p.K = K; p.lda = K; p.ldb = N; p.ldc = N; p.ldcin = N;
+        p.alpha = 1.0f; p.beta = 0.0f;
+        p.iters = clamp_gemm_iters(iters <= 0 ? g_iters.load() : iters);
+        st = launch_gemm(p, kNN, mode < 0 ? g_mode.load() : mode, 0, c.s);
+    }
+    return c.finish(st, false);
+}
+
+RAC_API void rac_matmul(float* A, float* B, float* C, int M, int N, int K) {
+    set_status(do_matmul(A, B, C, M, N, K, -1, -1), "rac_matmul");
+}
+RAC_API void rac_matmul_ex(const float* A, const float* B, float* C, int M, int N, int K,
+                           int iters, int mode) {
+    set_status(do_matmul(A, B, C, M, N, K, iters, mode), "rac_matmul_ex");
+}
+
+static int do_rotate(const float2* v, const float* th, float2* out, long long n, int iters,
+                     int literal) {
+    if (n < 0) return kErrInvalidDim;
+    if (n == 0) return kOk;
+    if (!v || !th || !out) return kErrNullPtr;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    auto dv = (const float2*)c.map(v, sizeof(float2) * n, true, false);
+    auto dt = (const float*)c.map(th, sizeof(float) * n, true, false);
+    auto dout = (float2*)c.map(out, sizeof(float2) * n, false, true);
+    int st = c.st == kOk ? rotate_batch(dv, dt, dout, n, iters, literal, c.s) : c.st;
+    return c.finish(st, true);
+}
+
+RAC_API void rac_rotate_batch(float2* v, float* theta, float2* out, int n) {
+    set_status(do_rotate(v, theta, out, n, kDefaultIters, 1), "rac_rotate_batch");
+}
+RAC_API void rac_rotate_batch_n(const float2* v, const float* theta, float2* out, int n, int iters) {
+    set_status(do_rotate(v, theta, out, n, iters, 0), "rac_rotate_batch_n");
+}
+RAC_API float2 rac_rotate(float2 v, float theta) {
+    float2 out = make_float2(0.f, 0.f);
+    set_status(do_rotate(&v, &theta, &out, 1, kDefaultIters, 1), "rac_rotate");
+    return out;
+}
+RAC_API float2 rac_rotate_precision(float2 v, float theta, int iters) {
+    float2 out = make_float2(0.f, 0.f);
+    set_status(do_rotate(&v, &theta, &out, 1, iters, 0), "rac_rotate_precision");
+    return out;
+}
+
+static int do_project(const float2* v, const float* th, float* out, long long n, int iters) {
+    if (n < 0) return kErrInvalidDim;
+    if (n == 0) return kOk;
+    if (!v || !th || !out) return kErrNullPtr;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    auto dv = (const float2*)c.map(v, sizeof(float2) * n, true, false);
+    auto dt = (const float*)c.map(th, sizeof(float) * n, true, false);
+    auto dout = (float*)c.map(out, sizeof(float) * n, false, true);
+    int st = c.st == kOk ? project_batch(dv, dt, dout, n, iters, c.s) : c.st;
+    return c.finish(st, true);
+}
+RAC_API void rac_project_batch_n(const float2* v, const float* theta, float* out, int n, int iters) {
+    set_status(do_project(v, theta, out, n, iters), "rac_project_batch_n");
+}
+RAC_API float rac_project_precision(float2 v, float theta, int iters) {
+    float out = 0.f;
+    set_status(do_project(&v, &theta, &out, 1, iters), "rac_project_precision");
+    return out;
+}
+
+static int do_unary(const float* x, float* y, long long n, int op) {
+    if (n < 0) return kErrInvalidDim;
+    if (n == 0) return kOk;
+    if (!x || !y) return kErrNullPtr;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    auto dx = (const float*)c.map(x, sizeof(float) * n, true, false);
+    auto dy = (float*)c.map(y, sizeof(float) * n, false, true);
+    int st = c.st == kOk ? unary_batch(dx, dy, n, op, c.s) : c.st;
+    return c.finish(st, false);
+}
+RAC_API void rac_exp_batch(const float* x, float* y, int n) { set_status(do_unary(x, y, n, kUnaryExp), "rac_exp_batch"); }
+RAC_API void rac_tanh_batch(const float* x, float* y, int n) { set_status(do_unary(x, y, n, kUnaryTanh), "rac_tanh_batch"); }
+RAC_API void rac_rsqrt_batch(const float* x, float* y, int n) { set_status(do_unary(x, y, n, kUnaryRsqrt), "rac_rsqrt_batch"); }
+RAC_API void rac_sigmoid_batch(const float* x, float* y, int n) { set_status(do_unary(x, y, n, kUnarySigmoid), "rac_sigmoid_batch"); }
+static float unary1(float x, int op, const char* name) {
+    float y = 0.f;
+    set_status(do_unary(&x, &y, 1, op), name);
+    return y;
+}
+RAC_API float rac_exp(float x) { return unary1(x, kUnaryExp, "rac_exp"); }
+RAC_API float rac_tanh(float x) { return unary1(x, kUnaryTanh, "rac_tanh"); }
+RAC_API float rac_rsqrt(float x) { return unary1(x, kUnaryRsqrt, "rac_rsqrt"); }
+RAC_API float rac_sigmoid(float x) { return unary1(x, kUnarySigmoid, "rac_sigmoid"); }
+
+RAC_API void rac_sincos_batch(const float* theta, float* s, float* c_out, int n) {
+    int st = kOk;
+    if (n < 0) st = kErrInvalidDim;
+    else if (n > 0 && (!theta || !s || !c_out)) st = kErrNullPtr;
+    else if (n > 0) {
+        Call c;
+        if (c.begin() == kOk) {
+            auto dt = (const float*)c.map(theta, sizeof(float) * n, true, false);
+            auto ds = (float*)c.map(s, sizeof(float) * n, false, true);
+            auto dc = (float*)c.map(c_out, sizeof(float) * n, false, true);
+            st = c.finish(c.st == kOk ? sincos_batch(dt, ds, dc, n, c.s) : c.st, true);
+        } else {
+            st = c.st;
+        }
+    }
+    set_status(st, "rac_sincos_batch");
+}
+RAC_API void rac_sincos(float theta, float* s, float* c) {
+    float ls = 0.f, lc = 0.f;
+    rac_sincos_batch(&theta, &ls, &lc, 1);
+    if (s) *s = ls;
+    if (c) *c = lc;
+}
+
+static int do_rows(int op, const float* x, float* y, const float* g, const float* b, float eps,
+                   long long rows, int d) {
+    if (rows < 0 || d <= 0) return kErrInvalidDim;
+    if (rows == 0) return kOk;
+    if (!x || !y) return kErrNullPtr;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    const size_t bytes = sizeof(float) * (size_t)rows * d;
+    auto dx = (const float*)c.map(x, bytes, true, false);
+    auto dy = (float*)c.map(y, bytes, false, true);
+    auto dg = (const float*)c.map(g, sizeof(float) * d, true, false);
+    auto db = (const float*)c.map(b, sizeof(float) * d, true, false);
+    int st = c.st;
+    if (st == kOk) {
+        if (op == 0) st = softmax_rows(dx, dy, rows, d, c.s);
+        else if (op == 1) st = rmsnorm_rows(dx, dy, dg, eps, rows, d, c.s);
+        else st = layernorm_rows(dx, dy, dg, db, eps, rows, d, c.s);
+    }
+    return c.finish(st, false);
+}
+RAC_API void rac_softmax(float* x, float* out, int n) {
+    set_status(do_rows(0, x, out, nullptr, nullptr, 0.f, 1, n), "rac_softmax");
+}
+RAC_API void rac_softmax_batch(const float* x, float* out, int batch, int n) {
+    set_status(do_rows(0, x, out, nullptr, nullptr, 0.f, batch, n), "rac_softmax_batch");
+}
+RAC_API void rac_rmsnorm(const float* x, float* y, const float* gamma, float eps, int rows, int d) {
+    set_status(do_rows(1, x, y, gamma, nullptr, eps, rows, d), "rac_rmsnorm");
+}
+RAC_API void rac_layernorm(const float* x, float* y, const float* gamma, const float* beta,
+                           float eps, int rows, int d) {
+    set_status(do_rows(2, x, y, gamma, beta, eps, rows, d), "rac_layernorm");
+}
+
+static int do_rope_cache(float* cos_out, float* sin_out, int max_seq, int hd, float base) {
+    if (!cos_out || !sin_out) return kErrNullPtr;
+    if (max_seq <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidDim;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    const size_t bytes = sizeof(float) * (size_t)max_seq * (hd / 2);
+    auto dc = (float*)c.map(cos_out, bytes, false, true);
+    auto ds = (float*)c.map(sin_out, bytes, false, true);
+    int st = c.st == kOk ? rope_cache(dc, ds, max_seq, hd, base, c.s) : c.st;
+    return c.finish(st, true);
+}
+RAC_API void rac_rope_cache(float* cos_out, float* sin_out, int max_seq, int head_dim, float base) {
+    set_status(do_rope_cache(cos_out, sin_out, max_seq, head_dim, base), "rac_rope_cache");
+}
+
+static int do_rope_apply(float* x, const float* ct, const float* sn, int batch, int heads, int seq,
+                         int hd) {
+    if (!x || !ct || !sn) return kErrNullPtr;
+    if (batch <= 0 || heads <= 0 || seq <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidDim;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    const size_t xb = sizeof(float) * (size_t)batch * heads * seq * hd;
+    const size_t tb = sizeof(float) * (size_t)seq * (hd / 2);
+    auto dx = (float*)c.map(x, xb, true, true);
+    auto dc = (const float*)c.map(ct, tb, true, false);
+    auto ds = (const float*)c.map(sn, tb, true, false);
+    int st = c.st == kOk ? rope_apply(dx, dc, ds, nullptr, (long long)batch * heads, seq, hd, 0, c.s) : c.st;
+    return c.finish(st, false);
+}
+RAC_API void rac_rope_apply(float* x, const float* cos_tab, const float* sin_tab, int batch,
+                            int n_heads, int seq, int head_dim) {
+    set_status(do_rope_apply(x, cos_tab, sin_tab, batch, n_heads, seq, head_dim), "rac_rope_apply");
+}
+
+// ── context API (rac.h:85-88) ───────────────────────────────────────────
+
+struct rac_context_t { rac_backend backend; int device; };
+
+RAC_API rac_context rac_create_context(rac_backend backend) {
+    if (backend != RAC_BACKEND_CUDA) { set_status(kErrUnsupported, "rac_create_context"); return nullptr; }
+    int dev = 0;
+    if (device_ready(&dev) != kOk) { set_status(kErrCuda, "rac_create_context"); return nullptr; }
+    auto* ctx = static_cast<rac_context>(std::malloc(sizeof(rac_context_t)));
+    if (!ctx) { set_status(kErrAlloc, "rac_create_context"); return nullptr; }
+    ctx->backend = backend;
+    ctx->device = dev;
+    set_status(kOk, "rac_create_context");
+    return ctx;
+}
+RAC_API void rac_destroy_context(rac_context ctx) { std::free(ctx); }
+
+RAC_API int rac_query_capability(rac_context ctx, rac_op_type op) {
+    (void)ctx;
+    switch (op) {
+        case RAC_OP_ROTATE: case RAC_OP_EXP: case RAC_OP_TANH: case RAC_OP_SOFTMAX:
+        case RAC_OP_ROTATE_BATCH: case RAC_OP_MATMUL: case RAC_OP_RSQRT: case RAC_OP_SIGMOID:
+        case RAC_OP_SINCOS: case RAC_OP_LAYERNORM: case RAC_OP_RMSNORM: case RAC_OP_ROPE_CACHE:
+        case RAC_OP_ROPE_APPLY:
+            return 1;
+        default:
+            return 0;
+    }
+}
+
+RAC_API int rac_execute(rac_context ctx, rac_op_type op, void* desc) {
+    if (!ctx || !desc) return set_status(kErrNullPtr, "rac_execute");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != ctx->device) cudaSetDevice(ctx->device);
+    switch (op) {
+        case RAC_OP_MATMUL: {
+            auto* d = static_cast<rac_matmul_desc*>(desc);
+            rac_matmul_ex(d->A, d->B, d->C, d->M, d->N, d->K, -1, -1);
+            break;
+        }
+        case RAC_OP_ROTATE_BATCH: {
+            auto* d = static_cast<rac_rotate_batch_desc*>(desc);
+            if (d->iters <= 0) rac_rotate_batch(const_cast<float2*>(d->v), const_cast<float*>(d->theta), d->out, d->n);
+            else rac_rotate_batch_n(d->v, d->theta, d->out, d->n, d->iters);
+            break;
+        }
+        case RAC_OP_SOFTMAX: {
+            auto* d = static_cast<rac_softmax_desc*>(desc);
+            rac_softmax_batch(d->x, d->out, d->rows, d->n);
+            break;
+        }
+        case RAC_OP_RMSNORM: {
+            auto* d = static_cast<rac_norm_desc*>(desc);
+            rac_rmsnorm(d->x, d->y, d->gamma, d->eps, d->rows, d->d);
+            break;
+        }
+        case RAC_OP_LAYERNORM: {
+            auto* d = static_cast<rac_norm_desc*>(desc);
+            rac_layernorm(d->x, d->y, d->gamma, d->beta, d->eps, d->rows, d->d);
+            break;
+        }
+        case RAC_OP_ROPE_APPLY: {
+            auto* d = static_cast<rac_rope_apply_desc*>(desc);
+            rac_rope_apply(d->x, d->cos_tab, d->sin_tab, d->batch, d->n_heads, d->seq, d->head_dim);
+            break;
+        }
+        case RAC_OP_ROPE_CACHE: {
+            auto* d = static_cast<rac_rope_cache_desc*>(desc);
+            rac_rope_cache(d->cos_out, d->sin_out, d->max_seq, d->head_dim, d->base);
+            break;
+        }
+        case RAC_OP_EXP: case RAC_OP_TANH: case RAC_OP_RSQRT: case RAC_OP_SIGMOID: {
+            auto* d = static_cast<rac_unary_desc*>(desc);
+            const int u = op == RAC_OP_EXP ? kUnaryExp : op == RAC_OP_TANH ? kUnaryTanh
+                        : op == RAC_OP_RSQRT ? kUnaryRsqrt : kUnarySigmoid;
+            set_status(do_unary(d->x, d->y, d->n, u), "rac_execute");
+            break;
+        }
+        default:
+            set_status(kErrUnsupported, "rac_execute");
+    }
+    const int st = t_status;
+    if (prev != ctx->device) cudaSetDevice(prev);
+    return st;
+}

@@ -1,0 +1,151 @@
+"""GPU parity of the rotation-accumulate GEMM (FAST and CORDIC modes).
+
+Each output accumulates sequentially over k exactly as the CPU restatement
+does (rac_torch/rac_kernels.hip:176-185, 239-425), so the comparison with
+oracle.gemm is bit-for-bit.  Against the CORDIC GEMM composed from lib/c's
+rac_project_n the bar is normwise max|diff| / rms(ref) <= 1e-4.
+"""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from rac_b200 import _lib, ext
+from rac_b200._lib import LAYOUT_NN, LAYOUT_NT, LAYOUT_TN
+
+pytestmark = pytest.mark.gpu
+NORM_TOL = 1e-4
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _normwise(got, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(np.asarray(got, np.float64) - ref).max() / max(math.sqrt(np.mean(ref * ref)), 1e-30))
+
+
+def _operands(M, N, K, layout, seed):
+    rng = np.random.default_rng(seed)
+    A = rng.uniform(-1, 1, (K, M) if layout == "tn" else (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (N, K) if layout == "nt" else (K, N)).astype(np.float32)
+    return A, B
+
+
+LAY = {"nn": LAYOUT_NN, "nt": LAYOUT_NT, "tn": LAYOUT_TN}
+
+
+@pytest.mark.parametrize("layout", ["nn", "nt", "tn"])
+@pytest.mark.parametrize("shape", [(1, 1, 1), (63, 65, 67), (127, 255, 131), (128, 128, 128),
+                                   (16, 200, 96), (33, 64, 40), (256, 384, 512)])
+@pytest.mark.parametrize("mode,iters", [(0, 24), (1, 8), (1, 16), (1, 24), (1, 5)])
+def test_gemm_bitexact_vs_restatement(cuda, orc, layout, shape, mode, iters):
+    M, N, K = shape
+    A, B = _operands(M, N, K, layout, M * 7 + N + K)
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], iters, mode).cpu().numpy()
+    want = orc.gemm(A, B, layout, mode, iters)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("iters", [8, 16, 24])
+def test_gemm_golden_composed(cuda, golden, iters):
+    A, B = golden["mm_A"], golden["mm_B"]
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAYOUT_NN, iters, 1).cpu().numpy()
+    assert _normwise(got, golden[f"mm_cordic{iters}"]) <= NORM_TOL
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAYOUT_NN, 24, 0).cpu().numpy()
+    assert _normwise(got, golden["mm_sgemm"]) <= NORM_TOL
+
+
+def test_rac_matmul_host_abi_default_knobs(cuda, orc):
+    """rac.h rac_matmul with host buffers: process knobs default to CORDIC, 16."""
+    L = _lib.lib()
+    L.rac_set_cordic_iters(0)
+    L.rac_set_cordic_mode(1)
+    A, B = _operands(70, 90, 110, "nn", 11)
+    C = np.zeros((70, 90), np.float32)
+    L.rac_matmul(_p(A), _p(B), _p(C), 70, 90, 110)
+    _lib.check()
+    assert np.array_equal(C, orc.gemm(A, B, "nn", 1, 16))
+    C2 = np.zeros_like(C)
+    L.rac_matmul_ex(_p(A), _p(B), _p(C2), 70, 90, 110, 8, 1)
+    _lib.check()
+    assert np.array_equal(C2, orc.gemm(A, B, "nn", 1, 8))
+
+
+def test_launchers_alpha_beta(cuda, orc):
+    """rac_launch_*_iters: C = alpha*AB + beta*C (rac_kernels.hip:790-797)."""
+    L = _lib.lib()
+    A, B = _operands(40, 48, 56, "nn", 3)
+    C0 = np.random.default_rng(4).standard_normal((40, 48)).astype(np.float32)
+    dA, dB, dC = _t(A, cuda), _t(B, cuda), _t(C0, cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    L.rac_launch_nn_iters(dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), 40, 48, 56,
+                          ctypes.c_float(0.5), ctypes.c_float(2.0), 16, 1, s)
+    _lib.check()
+    acc = orc.gemm(A, B, "nn", 1, 16)
+    want = (np.float32(0.5) * acc.astype(np.float64) + 2.0 * C0).astype(np.float32)
+    assert np.abs(dC.cpu().numpy() - want).max() <= 1e-6
+    dC2 = torch.zeros((40, 48), device=cuda)
+    L.rac_launch_nt(dA.data_ptr(), _t(np.ascontiguousarray(B.T), cuda).data_ptr(), dC2.data_ptr(),
+                    40, 48, 56, ctypes.c_float(1.0), ctypes.c_float(0.0), s)
+    _lib.check()
+    assert np.array_equal(dC2.cpu().numpy(), orc.gemm(A, B, "nn", 0, 24))
+
+
+@pytest.mark.parametrize("act", [1, 2, 3])
+def test_fused_bias_act_epilogue(cuda, orc, act):
+    A, W = _operands(37, 52, 64, "nt", act)
+    bias = np.random.default_rng(9).standard_normal(52).astype(np.float32)
+    got = ext.fused_linear_forward(_t(A, cuda), _t(W, cuda), _t(bias, cuda), act, 16, 1).cpu()
+    pre = torch.from_numpy(orc.gemm(A, W, "nt", 1, 16)) + torch.from_numpy(bias)
+    ref = {1: torch.relu, 2: lambda t: torch.nn.functional.gelu(t), 3: torch.nn.functional.silu}[act](pre)
+    assert torch.allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_residual_epilogue_and_strided_operands(cuda, orc):
+    A, W = _operands(64, 96, 128, "nt", 21)
+    R = np.random.default_rng(1).standard_normal((64, 96)).astype(np.float32)
+    got = ext.gemm(_t(A, cuda), _t(W, cuda), LAYOUT_NT, 16, 1, residual=_t(R, cuda)).cpu().numpy()
+    want = orc.gemm(A, W, "nt", 1, 16) + R
+    assert np.array_equal(got, want.astype(np.float32))
+    big = torch.zeros((64, 200), device=cuda)
+    big[:, 8:136] = _t(A, cuda)
+    view = big[:, 8:136]                                   # leading dim 200, 16B-aligned base
+    got2 = ext.gemm(view, _t(W, cuda), LAYOUT_NT, 16, 1).cpu().numpy()
+    assert np.array_equal(got2, orc.gemm(A, W, "nt", 1, 16))
+
+
+def test_large_sampled_rows_vs_oracle(cuda, orc):
+    """1024x2048x4096 at 16 iterations: sampled rows bit-exact to the restatement."""
+    M, N, K = 1024, 2048, 4096
+    g = torch.Generator(device="cpu").manual_seed(5)
+    A = (torch.rand((M, K), generator=g) * 2 - 1)
+    B = (torch.rand((K, N), generator=g) * 2 - 1)
+    C = ext.gemm(A.to(cuda), B.to(cuda), LAYOUT_NN, 16, 1).cpu().numpy()
+    An, Bn = A.numpy(), B.numpy()
+    for r in (0, 1, 63, 64, 511, 1023):
+        assert np.array_equal(C[r:r + 1], orc.gemm(An, Bn, "nn", 1, 16, rows=(r, r + 1))), r
+
+
+def test_cordic_equals_fast_on_rotated_operand(cuda):
+    """Size-independent property: since the direction sequence is data-independent
+    and rotation is odd-symmetric, CORDIC(A, B) == FAST(x_n(A)/K(n), B) bit-for-bit.
+    Checked at the full 4096^3 benchmark shape."""
+    M = N = K = 4096
+    g = torch.Generator(device=cuda).manual_seed(0)
+    A = torch.rand((M, K), device=cuda, generator=g) * 2 - 1
+    B = torch.rand((K, N), device=cuda, generator=g) * 2 - 1
+    C = ext.gemm(A, B, LAYOUT_NN, 16, 1)
+    # x_n(a)/K(n) for every a: a 1x1 CORDIC GEMM of a against b = 1
+    ones = torch.ones((1, 1), device=cuda)
+    Ar = ext.gemm(A.reshape(-1, 1), ones, LAYOUT_NN, 16, 1).reshape(M, K)
+    Cf = ext.gemm(Ar, B, LAYOUT_NN, 24, 0)
+    assert torch.equal(C, Cf)

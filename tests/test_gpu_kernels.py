@@ -1,0 +1,193 @@
+"""GPU parity of every kernel against the CPU oracle and the golden vectors.
+
+All calls go through the C ABI of librac_b200.so: the blocking rac.h entry
+points with host buffers, and the stream-ordered *_async entry points (via
+rac_b200.ext) with device tensors.  Bars:
+  * integer/bit work and the elementwise CORDIC ops: bit-exact to lib/c
+    (the golden vectors) -- stricter than the 2-ulp bar;
+  * GEMM: bit-exact to the sequential-k restatement, and normwise
+    max|diff|/rms(ref) <= 1e-4 to the CORDIC GEMM composed from lib/c's
+    rac_project_n;
+  * reductions (softmax, norms): max relative error <= 1e-4 with denominator
+    max(|ref|, 1e-3 * rms(ref)).
+"""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from rac_b200 import _lib, ext
+
+pytestmark = pytest.mark.gpu
+fp = ctypes.c_void_p
+
+
+def _p(a):
+    return a.ctypes.data_as(fp)
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _bits_equal(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+# ── elementwise CORDIC ──────────────────────────────────────────────────
+
+def test_rotate_batch_golden_host_abi(cuda, golden):
+    L = _lib.lib()
+    v, th = golden["rot_v"], golden["rot_theta"]
+    out = np.zeros_like(v)
+    L.rac_rotate_batch(_p(v), _p(th), _p(out), th.size)
+    _lib.check()
+    assert _bits_equal(out, golden["rot_batch"])
+
+
+@pytest.mark.parametrize("it", [4, 8, 12, 16, 24])
+def test_rotate_project_n_golden(cuda, golden, it):
+    L = _lib.lib()
+    v, th = golden["rot_v"], golden["rot_theta"]
+    out = np.zeros_like(v)
+    L.rac_rotate_batch_n(_p(v), _p(th), _p(out), th.size, it)
+    _lib.check()
+    assert _bits_equal(out, golden[f"rot_n{it}"])
+    got = ext.project_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
+    assert _bits_equal(got, golden[f"proj_n{it}"])
+
+
+@pytest.mark.parametrize("it", [8, 16, 24])
+def test_rotate_batch_large_random(cuda, orc, it):
+    rng = np.random.default_rng(it)
+    n = (1 << 20) + 3                        # ragged tail after the float4 path
+    v = rng.standard_normal((n, 2)).astype(np.float32)
+    th = rng.uniform(-math.pi, math.pi, n).astype(np.float32)
+    got = ext.rotate_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
+    want = orc.rotate_batch(v, th, it, False)
+    assert _bits_equal(got, want)
+    got = ext.rotate_batch(_t(v, cuda), _t(th, cuda), None).cpu().numpy()
+    assert _bits_equal(got, orc.rotate_batch(v, th, 16, True))
+
+
+def test_rotate_edge_cases(cuda, orc):
+    th = np.array([0.0, -0.0, np.pi, -np.pi, 50.0, -50.0, 1e4, np.nan, 1.5707964, -1.5707964],
+                  np.float32)
+    v = np.tile(np.array([[0.3, -1.7]], np.float32), (th.size, 1))
+    got = ext.rotate_batch(_t(v, cuda), _t(th, cuda), 16).cpu().numpy()
+    want = orc.rotate_batch(v, th, 16, False)
+    assert _bits_equal(got, want)
+    ext.check_device_errors()
+    # empty input is a no-op
+    e = torch.empty((0, 2), device=cuda)
+    assert ext.rotate_batch(e, torch.empty(0, device=cuda), 16).numel() == 0
+
+
+def test_wrap_limit_reports_error_instead_of_hanging(cuda):
+    """The reference loops forever for |theta| >= 2^25; the kernel stops and flags it."""
+    v = torch.ones((4, 2), device=cuda)
+    th = torch.tensor([1e30, 0.0, float("inf"), 1.0], device=cuda)
+    ext.rotate_batch(v, th, 16)
+    with pytest.raises(_lib.RacError):
+        ext.check_device_errors()
+    ext.check_device_errors()                # the error word was cleared
+
+
+def test_sincos_and_unary_golden(cuda, golden, orc):
+    L = _lib.lib()
+    x = golden["unary_x"]
+    for fn, key in ((L.rac_exp_batch, "exp_out"), (L.rac_tanh_batch, "tanh_out")):
+        y = np.zeros_like(x)
+        fn(_p(x), _p(y), x.size)
+        _lib.check()
+        assert (O.ulp_distance(y, golden[key]) <= 2).all(), key
+    xr = golden["rsqrt_x"]
+    y = ext.rsqrt(_t(xr, cuda)).cpu().numpy()
+    assert _bits_equal(y, golden["rsqrt_out"])
+    assert abs(L.rac_rsqrt(4.0) - 0.5) < 1e-6 and L.rac_rsqrt(0.0) == 0.0
+    assert abs(L.rac_sigmoid(0.0) - 0.5) < 1e-5 and L.rac_sigmoid(10.0) > 0.999
+    th = golden["rot_theta"]
+    s, c = ext.sincos(_t(th, cuda))
+    s_ref = np.zeros_like(th); c_ref = np.zeros_like(th)
+    for i in range(0, th.size, 97):
+        ss = ctypes.c_float(); cc = ctypes.c_float()
+        O.orc().orc_sincos(float(th[i]), ctypes.byref(ss), ctypes.byref(cc))
+        assert s.cpu().numpy()[i] == ss.value and c.cpu().numpy()[i] == cc.value
+
+
+# ── RoPE ────────────────────────────────────────────────────────────────
+
+def test_rope_cache_golden(cuda, golden):
+    c, s = ext.rope_cache(64, 128, 10000.0, device=cuda)
+    assert _bits_equal(c.cpu(), golden["rope_cos"]) and _bits_equal(s.cpu(), golden["rope_sin"])
+    c2, s2 = ext.rope_cache(4096, 128, 10000.0, device=cuda)
+    rows = golden["rope4096_rows"]
+    assert _bits_equal(c2.cpu().numpy()[rows], golden["rope4096_cos"])
+    assert _bits_equal(s2.cpu().numpy()[rows], golden["rope4096_sin"])
+
+
+def test_rope_apply_golden_and_host_abi(cuda, golden):
+    x = golden["rope_x"].copy()
+    L = _lib.lib()
+    L.rac_rope_apply(_p(x), _p(golden["rope_cos"]), _p(golden["rope_sin"]), *x.shape)
+    _lib.check()
+    assert _bits_equal(x, golden["rope_out"])
+    xt = _t(golden["rope_x"], cuda)
+    ext.rope_apply_(xt, _t(golden["rope_cos"], cuda), _t(golden["rope_sin"], cuda))
+    assert _bits_equal(xt.cpu(), golden["rope_out"])
+
+
+def test_rope_apply_odd_head_dim_scalar_path(cuda, orc):
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, 3, 17, 6)).astype(np.float32)
+    c, s = orc.rope_cache(17, 6, 500.0)
+    got = _t(x, cuda)
+    ext.rope_apply_(got, _t(c, cuda), _t(s, cuda))
+    assert _bits_equal(got.cpu(), orc.rope_apply(x, c, s))
+
+
+# ── row-wise ────────────────────────────────────────────────────────────
+
+@pytest.mark.parametrize("shape", [(9, 1000), (64, 4096), (3, 4097), (2, 8192), (1, 20000), (5, 1)])
+def test_softmax(cuda, orc, shape):
+    rng = np.random.default_rng(shape[1])
+    x = (rng.standard_normal(shape) * 3).astype(np.float32)
+    got = ext.softmax(_t(x, cuda)).cpu().numpy()
+    assert O.max_rel_err(got, orc.softmax(x)) <= 1e-4
+
+
+def test_softmax_golden_host_abi(cuda, golden):
+    x = golden["softmax_x"]
+    out = np.zeros_like(x)
+    _lib.lib().rac_softmax_batch(_p(x), _p(out), x.shape[0], x.shape[1])
+    _lib.check()
+    assert O.max_rel_err(out, golden["softmax_out"]) <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(5, 4096), (31, 4096), (7, 1003), (4, 16384), (2, 4)])
+def test_norms(cuda, orc, shape):
+    rng = np.random.default_rng(shape[1] + 1)
+    x = rng.standard_normal(shape).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, shape[1]).astype(np.float32)
+    b = (rng.standard_normal(shape[1]) * 0.1).astype(np.float32)
+    got = ext.rmsnorm(_t(x, cuda), _t(g, cuda), 1e-6).cpu().numpy()
+    assert O.max_rel_err(got, orc.rmsnorm(x, g, 1e-6)) <= 1e-4
+    got = ext.layernorm(_t(x, cuda), _t(g, cuda), _t(b, cuda), 1e-6).cpu().numpy()
+    assert O.max_rel_err(got, orc.layernorm(x, g, b, 1e-6)) <= 1e-4
+    got = ext.rmsnorm(_t(x, cuda), None, 1e-6).cpu().numpy()
+    assert O.max_rel_err(got, orc.rmsnorm(x, None, 1e-6)) <= 1e-4
+
+
+def test_norms_golden_host_abi(cuda, golden):
+    L = _lib.lib()
+    x, g, b = golden["norm_x"], golden["norm_g"], golden["norm_b"]
+    y = np.zeros_like(x)
+    L.rac_rmsnorm(_p(x), _p(y), _p(g), ctypes.c_float(1e-6), x.shape[0], x.shape[1])
+    _lib.check()
+    assert O.max_rel_err(y, golden["rms_out"]) <= 1e-4
+    L.rac_layernorm(_p(x), _p(y), _p(g), _p(b), ctypes.c_float(1e-6), x.shape[0], x.shape[1])
+    _lib.check()
+    assert O.max_rel_err(y, golden["ln_out"]) <= 1e-4
