@@ -105,7 +105,7 @@ k_gemm(const __grid_constant__ GemmParams p) {
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;   // m tiles on x (2^31 limit)
 
     // A: NN/NT store A[M,K] (k contiguous); TN stores A[K,M].
     // B: NN/TN store B[K,N] (n contiguous); NT stores B[N,K].
@@ -223,7 +223,7 @@ template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
 int launch_inst(const GemmParams& p, cudaStream_t s) {
     using T = TileCfg<V>;
     constexpr int NT = (T::BM / T::TM) * (T::BN / T::TN);
-    dim3 grid((p.N + T::BN - 1) / T::BN, (p.M + T::BM - 1) / T::BM);
+    dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN);
     if (grid.y > 65535) return kErrInvalidDim;
     k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC><<<grid, NT, 0, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;

@@ -1,0 +1,210 @@
+"""Multi-GPU layouts of the RAC hot path (one process per GPU, torch.distributed).
+
+* ``column_shard`` / ``sharded_matmul``: rac_matmul split by N-column blocks.
+  A is replicated, rank r owns B[:, n0:n1] and C[:, n0:n1]; there is no
+  exchange on the data path (the reference's MPI path splits M rows instead,
+  lib/c/rac_mpi.c:52-112; N-columns also balances the M=16 skinny case).
+  ``gather_columns`` is the optional NCCL all-gather of C.
+* ``TPLlamaBlock``: RACLlamaBlock with Megatron-style tensor parallelism --
+  qkv and the FFN up-projections split by output rows (whole heads / ff
+  slices per rank), out_proj and the down-projection split by input columns,
+  one NCCL all-reduce (sum, fp32) after each of the two row-split GEMMs.
+  Rank 0 adds the residual in its GEMM epilogue so the all-reduce yields
+  x + sum of partials directly.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import ext
+from .rac_torch import RACLlamaBlock, RACRoPEAttention, RACRMSNorm, _kw
+
+
+def column_shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """[n0, n1) columns owned by `rank` (sizes differ by at most one)."""
+    return n * rank // world, n * (rank + 1) // world
+
+
+def sharded_matmul(A: torch.Tensor, B_local: torch.Tensor, iters: int = 16, mode: int = 1,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """This rank's C[:, n0:n1] = A @ B[:, n0:n1]; no communication."""
+    return ext.gemm(A, B_local, ext.LAYOUT_NN, iters, mode, out=out)
+
+
+def gather_columns(C_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """All-gather of the column blocks into the full C (equal block sizes)."""
+    import torch.distributed as dist
+    parts = [torch.empty_like(C_local) for _ in range(world)]
+    dist.all_gather(parts, C_local.contiguous(), group=group)
+    return torch.cat(parts, dim=1)
+
+
+class TPLlamaBlock(nn.Module):
+    """One rank's shard of an RACLlamaBlock (inference forward)."""
+
+    def __init__(self, full: RACLlamaBlock, world: int, rank: int, group=None):
+        super().__init__()
+        a = full.attn
+        H, hd, d = a.n_heads, a.d_head, a.d_model
+        if H % world:
+            raise ValueError(f"n_heads={H} not divisible by world={world}")
+        self.world, self.rank, self.group = world, rank, group
+        self.h_local = H // world
+        h0, h1 = rank * self.h_local * hd, (rank + 1) * self.h_local * hd
+        dev = a.qkv.weight.device
+        self.norm1 = full.norm1
+        self.norm2 = full.norm2
+        self.attn = RACRoPEAttention(d, H, max_seq_len=a.rope.max_seq_len, bias=False,
+                                     rope_base=a.rope.base, device=dev)
+        self.attn.n_heads = self.h_local
+        wq = a.qkv.weight.data
+        with torch.no_grad():
+            self.attn.qkv = _linear_from(torch.cat([wq[h0:h1], wq[d + h0:d + h1],
+                                                    wq[2 * d + h0:2 * d + h1]], 0))
+            self.attn.out_proj = _linear_from(a.out_proj.weight.data[:, h0:h1])
+        self.gated = full.gated
+        f = full.ffn
+        if self.gated:
+            ff = f.up.out_features
+            f0, f1 = ff * rank // world, ff * (rank + 1) // world
+            self.w_gate = _linear_from(f.gate.weight.data[f0:f1])
+            self.w_up = _linear_from(f.up.weight.data[f0:f1])
+            self.w_down = _linear_from(f.down.weight.data[:, f0:f1])
+        else:
+            ff = f.fc1.out_features
+            f0, f1 = ff * rank // world, ff * (rank + 1) // world
+            self.act_id = f.fc1.act_id
+            self.w_fc1 = _linear_from(f.fc1.weight.data[f0:f1])
+            self.w_fc2 = _linear_from(f.fc2.weight.data[:, f0:f1])
+
+    def _allreduce(self, t):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, group=self.group)
+        return t
+
+    @torch.no_grad()
+    def forward(self, x, mask=None, is_causal=True, positions=None):
+        res = x if self.rank == 0 else None
+        ctx = self.attn._context(self.norm1(x), mask, is_causal, positions, n_heads=self.h_local)
+        h = self._allreduce(ext.linear_forward(ctx, self.attn.out_proj.weight, None,
+                                               residual=res, **_kw()))
+        n2 = self.norm2(h)
+        res = h if self.rank == 0 else None
+        if self.gated:
+            g = ext.linear_forward(n2, self.w_gate.weight, None, act=ext.ACT_SILU, **_kw())
+            u = ext.linear_forward(n2, self.w_up.weight, None, **_kw())
+            y = ext.linear_forward(g.mul_(u), self.w_down.weight, None, residual=res, **_kw())
+        else:
+            t = ext.linear_forward(n2, self.w_fc1.weight, None, act=self.act_id, **_kw())
+            y = ext.linear_forward(t, self.w_fc2.weight, None, residual=res, **_kw())
+        return self._allreduce(y)
+
+
+class _ShardLinear(nn.Module):
+    """A bias-free weight shard applied with the RAC GEMM (inference only)."""
+
+    def __init__(self, w: torch.Tensor):
+        super().__init__()
+        self.weight = nn.Parameter(w.contiguous().clone(), requires_grad=False)
+        self.bias = None
+
+    def forward(self, x):
+        return ext.linear_forward(x, self.weight, None, **_kw())
+
+
+def _linear_from(w: torch.Tensor) -> nn.Module:
+    return _ShardLinear(w)
+
+
+def make_block(d: int, H: int, ff: int, max_seq: int, gated: bool, device, seed: int = 0):
+    """RACLlamaBlock with the benchmark's random init: weights ~N(0, 0.02),
+    norm gains 1 (identical on every rank for a given seed)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    blk = RACLlamaBlock(d, H, ff_dim=ff, max_seq_len=max_seq, activation="silu", bias=False,
+                        gated=gated, device="meta")
+    blk = blk.to_empty(device=device)
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if p.dim() > 1:
+                p.copy_((torch.randn(p.shape, generator=g) * 0.02).to(device))
+            else:
+                p.fill_(1.0)
+    # rebuild the RoPE caches (to_empty left them uninitialised)
+    from .rac_torch import RACRoPE
+    blk.attn.rope = RACRoPE(d // H, max_seq_len=max_seq, base=10000.0, device=device)
+    return blk
+
+
+def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler) -> dict | None:
+    """RACLlamaBlock tokens/s: d 4096, 32 heads, ff 11008 SwiGLU, x [4, 2048, 4096],
+    CORDIC 16 iterations (or --mode fast), tensor-parallel over `world` ranks."""
+    import statistics
+    import time
+
+    from . import rac_torch as R
+    dev = torch.device("cuda", local)
+    R.rac_set_mode("cordic" if args.mode == "cordic" else "fast")
+    R.rac_set_precision(args.iters)
+    d, H, ff, Bt, T = 4096, 32, 11008, 4, 2048
+    if args.size != 4096:            # reduced shape for quick checks
+        d, H, ff, Bt, T = args.size, max(1, args.size // 128), int(args.size * 2.6875), 2, 256
+    full = make_block(d, H, ff, max(T, 64), True, dev)
+    blk = TPLlamaBlock(full, world, rank)
+    del full
+    torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(99)
+    x = torch.randn((Bt, T, d), device=dev, generator=g)
+    for _ in range(args.warmup):
+        blk(x)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            starts[i].record(s)
+            blk(x)
+            ends[i].record(s)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
+    t = max_over_ranks(t_local, world)
+    # e2e: pinned host input -> device, forward, result back to the host.
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    ts = []
+    for _ in range(max(1, min(args.steps, 3))):
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(blk(xd), non_blocking=True)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+    te = max_over_ranks(statistics.mean(ts), world)
+    if rank != 0:
+        return None
+    tokens = Bt * T
+    macs = tokens * (4 * d * d + 3 * d * ff) // world            # projections, per rank
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = 1965.0
+    peak_mac = sms * 128 * mhz * 1e6 / (2 * args.iters + 2) if args.mode == "cordic" else sms * 128 * mhz * 1e6
+    return {
+        "metric": "RACLlamaBlock tokens/s", "value": tokens / (t * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights ~N(0,0.02))",
+        "config": {"workload": f"RACLlamaBlock d={d} H={H} ff={ff} SwiGLU, x [{Bt},{T},{d}], causal, "
+                               f"{args.mode} {args.iters if args.mode == 'cordic' else ''}",
+                   "parallelism": f"tp{world}", "l2": "inputs and weights larger than L2"},
+        "roofline": {"bound": "fp32_issue", "achieved": macs / (t_local * 1e-3) / 1e12,
+                     "peak": peak_mac / 1e12, "unit": "TMAC/s (projection GEMMs only)",
+                     "frac": macs / (t_local * 1e-3) / peak_mac, "traffic": None},
+        "e2e": {"value": tokens / te, "unit": "tokens/s", "h2d_bytes_per_step": 4 * x.numel(),
+                "d2h_bytes_per_step": 4 * x.numel()},
+        "gpu_launches": None, "clocks": clk.summary(),
+    }
