@@ -30,6 +30,9 @@ sys.path.insert(0, ROOT)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
+# ~0.5 ms device spin queued ahead of each timed launch, so that the host's
+# launch latency (Python + ctypes) is not inside the CUDA-event interval.
+SPIN_CYCLES = 1_000_000
 
 
 def load_peaks() -> dict:
@@ -261,6 +264,7 @@ def run_matmul(args, world, rank, local) -> dict | None:
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             flush.zero_()                              # between steps, outside the events
+            torch.cuda._sleep(SPIN_CYCLES)
             starts[i].record(s)
             step()
             ends[i].record(s)
@@ -330,8 +334,8 @@ def run_stream(args, world, rank, local) -> dict | None:
         cfg = f"rac_rotate_batch_n 2^26 float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
     elif w == "rope":
         q = torch.randn((8, 32, 4096, 128), device=dev, generator=g)
-        c, s = ext.rope_cache(4096, 128, 10000.0, device=dev)
-        fn = lambda: ext.rope_apply_(q, c, s)                     # noqa: E731
+        ctab, stab = ext.rope_cache(4096, 128, 10000.0, device=dev)
+        fn = lambda: ext.rope_apply_(q, ctab, stab)               # noqa: E731
         bytes_, units, unit_name = 8 * q.numel(), q.numel(), "Gelem/s"
         cfg = "rac_rope_apply Q [8,32,4096,128] fp32 in place, base 1e4"
     elif w == "softmax":
@@ -362,6 +366,7 @@ def run_stream(args, world, rank, local) -> dict | None:
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             flush.zero_()
+            torch.cuda._sleep(SPIN_CYCLES)          # keeps the GPU busy while the host enqueues
             starts[i].record(s)
             fn()
             ends[i].record(s)

@@ -9,7 +9,9 @@ rac_b200.ext) with device tensors.  Bars:
     max|diff|/rms(ref) <= 1e-4 to the CORDIC GEMM composed from lib/c's
     rac_project_n;
   * reductions (softmax, norms): max relative error <= 1e-4 with denominator
-    max(|ref|, 1e-3 * rms(ref)).
+    max(|ref|, 1e-3 * rms(ref)); for LayerNorm, whose float32 reference is
+    itself ~1.8e-4 from the exact result under that metric, the bar of
+    oracle.reduction_ok (no farther from exact than the reference).
 """
 import ctypes
 import math
@@ -176,7 +178,10 @@ def test_norms(cuda, orc, shape):
     got = ext.rmsnorm(_t(x, cuda), _t(g, cuda), 1e-6).cpu().numpy()
     assert O.max_rel_err(got, orc.rmsnorm(x, g, 1e-6)) <= 1e-4
     got = ext.layernorm(_t(x, cuda), _t(g, cuda), _t(b, cuda), 1e-6).cpu().numpy()
-    assert O.max_rel_err(got, orc.layernorm(x, g, b, 1e-6)) <= 1e-4
+    xd = x.astype(np.float64)
+    m = xd.mean(1, keepdims=True)
+    exact = g * (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
+    assert O.reduction_ok(got, orc.layernorm(x, g, b, 1e-6), exact)
     got = ext.rmsnorm(_t(x, cuda), None, 1e-6).cpu().numpy()
     assert O.max_rel_err(got, orc.rmsnorm(x, None, 1e-6)) <= 1e-4
 
@@ -190,4 +195,7 @@ def test_norms_golden_host_abi(cuda, golden):
     assert O.max_rel_err(y, golden["rms_out"]) <= 1e-4
     L.rac_layernorm(_p(x), _p(y), _p(g), _p(b), ctypes.c_float(1e-6), x.shape[0], x.shape[1])
     _lib.check()
-    assert O.max_rel_err(y, golden["ln_out"]) <= 1e-4
+    xd = x.astype(np.float64)
+    m = xd.mean(1, keepdims=True)
+    exact = g * (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
+    assert O.reduction_ok(y, golden["ln_out"], exact)
