@@ -182,6 +182,46 @@ def cpu_matmul_baseline(M: int, N: int, K: int, iters: int, reps: int = 1, warm:
     return out
 
 
+def cpu_stream_baseline(w: str, iters: int) -> dict | None:
+    """The reference lib/c op on the host cores, on a bounded sample of the workload."""
+    import numpy as np
+    import oracle as O
+    if not O.ref_available():
+        return None
+    rng = np.random.default_rng(3)
+    cores = os.cpu_count() or 1
+    if w == "rotate":
+        n = 1 << 22
+        v = rng.standard_normal((n, 2)).astype(np.float32)
+        th = rng.uniform(-np.pi, np.pi, n).astype(np.float32)
+        f = (lambda: O.ref_rotate_batch(v, th)) if iters == 16 else None
+        if f is None:
+            return None
+        units, unit, sample = n, "Gvec/s", f"2^22 vectors, lib/c rac_rotate_batch (16 iterations, OpenMP)"
+    elif w == "rope":
+        x = rng.standard_normal((1, 32, 4096, 128)).astype(np.float32)
+        c, s_ = O.ref_rope_cache(4096, 128, 10000.0)
+        f = lambda: O.ref_rope_apply(x, c, s_)                    # noqa: E731
+        units, unit, sample = x.size, "Gelem/s", "[1,32,4096,128], lib/c rac_rope_apply (incl. one copy)"
+    elif w == "softmax":
+        x = (rng.standard_normal((4096, 4096)) * 3).astype(np.float32)
+        f = lambda: O.ref_softmax(x)                              # noqa: E731
+        units, unit, sample = x.size, "Gelem/s", "4096 rows x 4096, lib/c rac_softmax_batch"
+    else:
+        x = rng.standard_normal((4096, 4096)).astype(np.float32)
+        g = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
+        b = (rng.standard_normal(4096) * 0.1).astype(np.float32)
+        f = (lambda: O.ref_rmsnorm(x, g, 1e-6)) if w == "rmsnorm" else (lambda: O.ref_layernorm(x, g, b, 1e-6))
+        units, unit, sample = x.size, "Gelem/s", f"4096 rows x 4096, lib/c rac_{w}"
+    f()
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        f()
+    t = (time.perf_counter() - t0) / reps
+    return {"value": units / t / 1e9, "unit": unit, "cores": cores, "kind": "reference", "sample": sample}
+
+
 def run_reference(args) -> None:
     """--impl reference: the reference's own CPU rac_matmul on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -238,6 +278,8 @@ def run_matmul(args, world, rank, local) -> dict | None:
     import torch
     from rac_b200 import _lib, ext
     M = N = K = args.size
+    if args.shape:
+        M, N, K = (int(v) for v in args.shape.split(","))
     iters = args.iters
     mode = 0 if args.mode == "fast" else 1
     n0, n1 = N * rank // world, N * (rank + 1) // world
@@ -300,7 +342,8 @@ def run_matmul(args, world, rank, local) -> dict | None:
     peaks = load_peaks()
     traffic = load_traffic().get(f"gemm_cordic{iters}_{M}")
     out = {
-        "metric": "rac_matmul MAC-equiv GOP/s at 4096^3" if M == 4096 else f"rac_matmul MAC-equiv GOP/s at {M}^3",
+        "metric": "rac_matmul MAC-equiv GOP/s at 4096^3" if M == N == K == 4096
+                  else f"rac_matmul MAC-equiv GOP/s at {M}x{N}x{K}",
         "value": value, "unit": "GOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -312,10 +355,19 @@ def run_matmul(args, world, rank, local) -> dict | None:
         "e2e": {"value": 2.0 * M * N * K / te / 1e9, "unit": "GOP/s",
                 "h2d_bytes_per_step": 4 * (M * K + K * Nl), "d2h_bytes_per_step": 4 * M * Nl,
                 "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if _splits(M, N // world, K, sms) > 1 else 1),
         "clocks": clk.summary(),
     }
     return out
+
+
+def _splits(M: int, N: int, K: int, sms: int) -> int:
+    """Mirror of the library's split-K rule (gemm_dispatch.cu splitk_count)."""
+    bm, bn = (16, 128) if M <= 32 else (64, 128)
+    tiles = -(-M // bm) * -(-N // bn)
+    if tiles >= sms or K < 1024:
+        return 1
+    return max(1, min(-(-4 * sms // tiles), K // 256))
 
 
 def run_stream(args, world, rank, local) -> dict | None:
@@ -379,7 +431,9 @@ def run_stream(args, world, rank, local) -> dict | None:
     peaks = load_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
     ach = bytes_ / (t_local * 1e-3) / 1e9
+    cpu = cpu_stream_baseline(w, args.iters) if (world == 1 and not args.no_cpu_baseline) else None
     return {
+        "cpu_baseline": cpu,
         "metric": f"{w} throughput", "value": units * world / (t * 1e-3) / 1e9, "unit": unit_name,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -402,6 +456,7 @@ def main() -> None:
     ap.add_argument("--workload", default="matmul",
                     choices=["matmul", "rotate", "rope", "softmax", "rmsnorm", "layernorm", "llama"])
     ap.add_argument("--size", type=int, default=4096)
+    ap.add_argument("--shape", default=None, help="M,N,K for the matmul workload (e.g. 16,11008,4096)")
     ap.add_argument("--iters", type=int, default=16)
     ap.add_argument("--mode", choices=["cordic", "fast"], default="cordic")
     ap.add_argument("--variant", type=int, default=0)
@@ -422,7 +477,11 @@ def main() -> None:
         out = run_stream(args, world, rank, local)
     if rank == 0 and out is not None:
         if world == 1 and not args.no_cpu_baseline and args.workload == "matmul":
-            out["cpu_baseline"] = cpu_matmul_baseline(args.size, args.size, args.size, args.iters)
+            if args.shape:
+                M, N, K = (int(v) for v in args.shape.split(","))
+            else:
+                M = N = K = args.size
+            out["cpu_baseline"] = cpu_matmul_baseline(M, N, K, args.iters)
         print(json.dumps(out))
     if world > 1:
         import torch.distributed as dist

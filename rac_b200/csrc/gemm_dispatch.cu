@@ -1,4 +1,6 @@
 // gemm_dispatch.cu -- picks the GEMM kernel instance for a call.
+#include <mutex>
+
 #include "gemm_kernel.cuh"
 
 namespace racb {
@@ -39,13 +41,120 @@ static int pick_fixed(const GemmParams& p, int layout, int v, cudaStream_t s) {
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+static int sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+void keep_device_pool() {
+    static std::once_flag once[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return; }
+    std::call_once(once[dev], [dev] {
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+            unsigned long long thr = ~0ull;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+        }
+        cudaGetLastError();
+    });
+}
+
+static int tile_variant(const GemmParams& p, int variant) {
+    if (variant == 1 || variant == 3) return variant;
+    return p.M <= 32 ? 3 : 1;
+}
+
+// Split-K when the output tiles cannot fill the machine: fewer tiles than
+// SMs and K long enough that each chunk keeps >= 256 k-steps.  Target about
+// 4 resident CTAs per SM.  variant 10+S forces S splits (tests, sweeps).
+int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
+    (void)layout; (void)mode;
+    const int v = tile_variant(p, variant);
+    const int bm = v == 3 ? TileCfg<3>::BM : TileCfg<1>::BM;
+    const int bn = v == 3 ? TileCfg<3>::BN : TileCfg<1>::BN;
+    const long long tiles = (long long)((p.M + bm - 1) / bm) * ((p.N + bn - 1) / bn);
+    int S = 1;
+    if (variant >= 10) {
+        S = variant - 10;
+    } else if (variant == 0 && tiles < sm_count() && p.K >= 1024) {
+        const long long target = 4LL * sm_count();
+        S = (int)((target + tiles - 1) / tiles);
+        if (S > p.K / 256) S = p.K / 256;
+    }
+    if (S < 1) S = 1;
+    if (S > p.K) S = p.K;
+    return S;
+}
+
+__global__ void __launch_bounds__(256) k_splitk_reduce(const GemmParams p) {
+    const long long mn = (long long)p.M * p.N;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < mn;
+         e += (long long)gridDim.x * blockDim.x) {
+        float acc = p.ws[e];
+        for (int z = 1; z < p.splits; ++z) acc = __fadd_rn(acc, p.ws[z * mn + e]);
+        const int gm = (int)(e / p.N), gn = (int)(e % p.N);
+        float v;
+        if (p.beta != 0.0f)
+            v = __fmaf_rn(p.alpha, acc, __fmul_rn(p.beta, p.Cin[(long long)gm * p.ldcin + gn]));
+        else
+            v = __fmul_rn(p.alpha, acc);
+        if (p.bias) v = __fadd_rn(v, p.bias[gn]);
+        if (p.act) v = apply_act(v, p.act);
+        p.C[(long long)gm * p.ldc + gn] = v;
+    }
+}
+
+int launch_splitk_reduce(const GemmParams& p, cudaStream_t s) {
+    const long long mn = (long long)p.M * p.N;
+    long long blocks = (mn + 255) / 256;
+    const long long cap = 8LL * sm_count();
+    if (blocks > cap) blocks = cap;
+    k_splitk_reduce<<<(int)blocks, 256, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+
 int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
     if (p_in.M <= 0 || p_in.N <= 0 || p_in.K <= 0) return kErrInvalidDim;
     if (!p_in.A || !p_in.B || !p_in.C) return kErrNullPtr;
     if (layout < kNN || layout > kTN) return kErrUnsupported;
     if (p_in.beta != 0.0f && !p_in.Cin) return kErrNullPtr;
+    const int S = splitk_count(p_in, layout, mode, variant);
+    if (S <= 1) {
+        GemmParams p = p_in;
+        p.ws = nullptr; p.splits = 1; p.kchunk = 0;
+        return launch_gemm_into(p, layout, mode, variant, s);
+    }
+    // Workspace from the device's stream-ordered pool (cached across calls).
+    keep_device_pool();
     GemmParams p = p_in;
-    const int v = (variant == 1 || variant == 3) ? variant : (p.M <= 32 ? 3 : 1);
+    p.kchunk = ((p.K + S - 1) / S + 7) / 8 * 8;             // multiple of BK
+    p.splits = (p.K + p.kchunk - 1) / p.kchunk;
+    const size_t bytes = sizeof(float) * (size_t)p.splits * p.M * p.N;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&p.ws), bytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        return kErrAlloc;
+    }
+    int st = launch_gemm_into(p, layout, mode, variant, s);
+    if (st == kOk) st = launch_splitk_reduce(p, s);
+    cudaFreeAsync(p.ws, s);
+    return st;
+}
+
+// Launches the tile kernel for p as given (p.ws / p.splits / p.kchunk set by
+// the caller: ws == nullptr means no split).
+int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
+    GemmParams p = p_in;
+    const int v = tile_variant(p, variant);
     // Vector loads need 16-byte aligned bases, leading dims that are
     // multiples of 4 and contiguous extents that are multiples of 4.
     const int a_contig = (layout == kTN) ? p.M : p.K;

@@ -105,6 +105,9 @@ k_gemm(const __grid_constant__ GemmParams p) {
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
+    // K range of this CTA: all of K, or one split-K chunk (kchunk % BK == 0).
+    const int kbeg = p.ws ? blockIdx.z * p.kchunk : 0;
+    const int kend = p.ws ? min(p.K, kbeg + p.kchunk) : p.K;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;   // m tiles on x (2^31 limit)
 
     // A: NN/NT store A[M,K] (k contiguous); TN stores A[K,M].
@@ -115,10 +118,10 @@ k_gemm(const __grid_constant__ GemmParams p) {
     TileLoader<B_KCOLS ? BN : BK, B_KCOLS ? BK : BN, NT, VEC> lb;
 
     auto load_tiles = [&](int k0) {
-        if constexpr (A_KCOLS) la.load(p.A, p.lda, m0, k0, p.M, p.K, tid);
-        else                   la.load(p.A, p.lda, k0, m0, p.K, p.M, tid);
-        if constexpr (B_KCOLS) lb.load(p.B, p.ldb, n0, k0, p.N, p.K, tid);
-        else                   lb.load(p.B, p.ldb, k0, n0, p.K, p.N, tid);
+        if constexpr (A_KCOLS) la.load(p.A, p.lda, m0, k0, p.M, kend, tid);
+        else                   la.load(p.A, p.lda, k0, m0, kend, p.M, tid);
+        if constexpr (B_KCOLS) lb.load(p.B, p.ldb, n0, k0, p.N, kend, tid);
+        else                   lb.load(p.B, p.ldb, k0, n0, kend, p.N, tid);
     };
     auto store_tiles = [&](int buf) {
         la.template store<A_KCOLS, BM>(As[buf], tid);
@@ -132,15 +135,15 @@ k_gemm(const __grid_constant__ GemmParams p) {
         for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
     const float k_inv = p.k_inv;
-    const int ktiles = (p.K + BK - 1) / BK;
+    const int ktiles = (kend - kbeg + BK - 1) / BK;
 
-    load_tiles(0);
+    load_tiles(kbeg);
     store_tiles(0);
     __syncthreads();
 
     for (int kt = 0; kt < ktiles; ++kt) {
         const int buf = kt & 1;
-        if (kt + 1 < ktiles) load_tiles((kt + 1) * BK);   // in flight during compute
+        if (kt + 1 < ktiles) load_tiles(kbeg + (kt + 1) * BK);   // in flight during compute
 
         const float* __restrict__ Asb = As[buf];
         const float* __restrict__ Bsb = Bs[buf];
@@ -190,6 +193,20 @@ k_gemm(const __grid_constant__ GemmParams p) {
         __syncthreads();
     }
 
+    if (p.ws) {   // split-K partial: raw sums, the reduction applies the epilogue
+        float* w = p.ws + (long long)blockIdx.z * p.M * p.N;
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int gm = m0 + ty * TM + i;
+            if (gm >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; ++j) {
+                const int gn = n0 + tx * TN + j;
+                if (gn < p.N) w[(long long)gm * p.N + gn] = acc[i][j];
+            }
+        }
+        return;
+    }
     // Epilogue (rac_kernels.hip:790-797 for alpha/beta; rac_torch.cu:769-776
     // for bias + activation).
 #pragma unroll
@@ -223,7 +240,7 @@ template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
 int launch_inst(const GemmParams& p, cudaStream_t s) {
     using T = TileCfg<V>;
     constexpr int NT = (T::BM / T::TM) * (T::BN / T::TN);
-    dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN);
+    dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN, p.ws ? p.splits : 1);
     if (grid.y > 65535) return kErrInvalidDim;
     k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC><<<grid, NT, 0, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;

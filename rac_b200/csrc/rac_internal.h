@@ -36,13 +36,33 @@ struct GemmParams {
     int iters;            // CORDIC iteration count (runtime-iteration kernels)
     float k_inv;          // 1/K(iters)
     float coef[24];       // d_i * 2^-i (runtime-iteration kernels)
+    // Split-K: when ws != nullptr, CTA z accumulates k in [z*kchunk, (z+1)*kchunk)
+    // and stores its raw partial sums to ws[z][M][N]; a second kernel sums the
+    // partials in z order and applies the epilogue.
+    float* ws;
+    int kchunk;
+    int splits;
 };
+
+// launch_gemm without the split-K decision: launches the tile kernel for p
+// as given (p.ws == nullptr: whole K per CTA).
+int launch_gemm_into(const GemmParams& p, int layout, int mode, int variant,
+                     cudaStream_t stream);
+// Sums ws[0..splits-1][M][N] in order and applies the GEMM epilogue of p.
+int launch_splitk_reduce(const GemmParams& p, cudaStream_t stream);
+// Number of K splits launch_gemm uses for this problem (1 = none).
+int splitk_count(const GemmParams& p, int layout, int mode, int variant);
 
 // Launches one GEMM on `stream`. variant 0 = automatic tile choice; the other
 // values select a fixed tile (used by the tile sweep in the benchmark).
 // Returns a Status; never synchronises.
 int launch_gemm(const GemmParams& p, int layout, int mode, int variant,
                 cudaStream_t stream);
+
+// Makes the current device's default stream-ordered pool keep freed memory
+// (release threshold = max) so that workspaces and staging buffers are not
+// re-mapped on every call.  Idempotent, once per device.
+void keep_device_pool();
 
 // Per-device error word that bounded device loops set (see rac_device.cuh).
 unsigned int* device_error_word(int device);

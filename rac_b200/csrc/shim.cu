@@ -83,22 +83,6 @@ cudaStream_t call_stream(int dev) {
     return streams[dev];
 }
 
-// Staging buffers come from the device's stream-ordered pool.  By default the
-// pool returns freed memory to the driver at every synchronisation, which
-// makes each blocking call pay for fresh mappings; keep it instead.
-void keep_pool(int dev) {
-    static std::once_flag once[64];
-    if (dev < 0 || dev >= 64) return;
-    std::call_once(once[dev], [dev] {
-        cudaMemPool_t pool;
-        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-            unsigned long long thr = ~0ull;
-            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
-        }
-        cudaGetLastError();
-    });
-}
-
 bool is_device_ptr(const void* p) {
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) { cudaGetLastError(); return false; }
@@ -123,7 +107,7 @@ struct Call {
 
     int begin() {
         st = device_ready(&dev);
-        if (st == kOk) keep_pool(dev);
+        if (st == kOk) keep_device_pool();
         if (st == kOk) s = call_stream(dev);
         if (st == kOk && !s) st = kErrCuda;
         return st;

@@ -149,3 +149,33 @@ def test_cordic_equals_fast_on_rotated_operand(cuda):
     Ar = ext.gemm(A.reshape(-1, 1), ones, LAYOUT_NN, 16, 1).reshape(M, K)
     Cf = ext.gemm(Ar, B, LAYOUT_NN, 24, 0)
     assert torch.equal(C, Cf)
+
+
+def test_splitk_skinny_config(cuda, orc):
+    """The BASELINE skinny shape M=16, N=11008, K=4096 runs split-K (86 output
+    tiles on 148 SMs): normwise <= 1e-5 to the sequential restatement,
+    deterministic across calls."""
+    M, N, K = 16, 11008, 4096
+    rng = np.random.default_rng(16)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    dA, dB = _t(A, cuda), _t(B, cuda)
+    C1 = ext.gemm(dA, dB, LAYOUT_NN, 16, 1)
+    C2 = ext.gemm(dA, dB, LAYOUT_NN, 16, 1)
+    assert torch.equal(C1, C2)
+    want = orc.gemm(A, B, "nn", 1, 16)
+    assert _normwise(C1.cpu().numpy(), want) <= 1e-5
+    C3 = ext.gemm(dA, dB, LAYOUT_NN, 16, 1, variant=3)      # no split
+    assert np.array_equal(C3.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("layout", ["nn", "nt", "tn"])
+def test_splitk_forced_with_epilogue(cuda, orc, layout):
+    M, N, K = 63, 65, 1100
+    A, B = _operands(M, N, K, layout, 77)
+    bias = np.random.default_rng(3).standard_normal(N).astype(np.float32)
+    R = np.random.default_rng(4).standard_normal((M, N)).astype(np.float32)
+    kw = dict(bias=_t(bias, cuda), act=3, residual=_t(R, cuda))
+    ref = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=1, **kw).cpu().numpy()
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=13, **kw).cpu().numpy()
+    assert _normwise(got, ref) <= 1e-5
