@@ -365,6 +365,8 @@ def _splits(M: int, N: int, K: int, sms: int) -> int:
     """Mirror of the library's split-K rule (gemm_dispatch.cu splitk_count)."""
     bm, bn = (16, 128) if M <= 32 else (64, 128)
     tiles = -(-M // bm) * -(-N // bn)
+    if M > 32 and tiles < 8 * sms:
+        tiles = -(-M // 64) * -(-N // 64)            # 64x64 tiles
     if tiles >= sms or K < 1024:
         return 1
     return max(1, min(-(-4 * sms // tiles), K // 256))
@@ -378,12 +380,12 @@ def run_stream(args, world, rank, local) -> dict | None:
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     w = args.workload
     if w == "rotate":
-        n = 1 << 26
+        n = 1 << args.log2n
         v = torch.randn((n, 2), device=dev, generator=g)
         th = (torch.rand(n, device=dev, generator=g) * 2 - 1) * 3.14159265
         fn = lambda: ext.rotate_batch(v, th, args.iters)          # noqa: E731
         bytes_, units, unit_name = 20 * n, n, "Gvec/s"
-        cfg = f"rac_rotate_batch_n 2^26 float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
+        cfg = f"rac_rotate_batch_n 2^{args.log2n} float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
     elif w == "rope":
         q = torch.randn((8, 32, 4096, 128), device=dev, generator=g)
         ctab, stab = ext.rope_cache(4096, 128, 10000.0, device=dev)
@@ -460,6 +462,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=16)
     ap.add_argument("--mode", choices=["cordic", "fast"], default="cordic")
     ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--log2n", type=int, default=26, help="rotate workload: log2 of the vector count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -12,7 +12,8 @@ E4(kFast, 0, kNN) E4(kFast, 0, kNT) E4(kFast, 0, kTN)
 E4(kCordic, 0, kNN) E4(kCordic, 0, kNT) E4(kCordic, 0, kTN)
 #define E2(ITERS) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 1, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 1, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 3, true) \
-    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 3, true)
+    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 3, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 2, true) \
+    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 2, true)
 E2(8) E2(16) E2(24)
 
 template <int MODE, int ITERS, int LAYOUT>
@@ -35,6 +36,8 @@ static int pick_layout(const GemmParams& p, int layout, int v, bool vec, cudaStr
 
 template <int ITERS>
 static int pick_fixed(const GemmParams& p, int layout, int v, cudaStream_t s) {
+    if (v == 2) return layout == kNN ? launch_inst<kCordic, ITERS, kNN, 2, true>(p, s)
+                                     : launch_inst<kCordic, ITERS, kNT, 2, true>(p, s);
     if (layout == kNN) return pick_tile<kCordic, ITERS, kNN>(p, v, true, s);
     return pick_tile<kCordic, ITERS, kNT>(p, v, true, s);
 }
@@ -68,9 +71,15 @@ void keep_device_pool() {
     });
 }
 
+static int sm_count();
+
+// 3 for M <= 32; 2 when 64x128 tiles would fill fewer than two rounds of the
+// resident slots (4 per SM); 1 otherwise.  Variants 1-3 can be forced.
 static int tile_variant(const GemmParams& p, int variant) {
-    if (variant == 1 || variant == 3) return variant;
-    return p.M <= 32 ? 3 : 1;
+    if (variant >= 1 && variant <= 3) return variant;
+    if (p.M <= 32) return 3;
+    const long long tiles = (long long)((p.M + 63) / 64) * ((p.N + 127) / 128);
+    return tiles < 8LL * sm_count() ? 2 : 1;
 }
 
 // Split-K when the output tiles cannot fill the machine: fewer tiles than
@@ -80,7 +89,7 @@ int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
     (void)layout; (void)mode;
     const int v = tile_variant(p, variant);
     const int bm = v == 3 ? TileCfg<3>::BM : TileCfg<1>::BM;
-    const int bn = v == 3 ? TileCfg<3>::BN : TileCfg<1>::BN;
+    const int bn = v == 3 ? TileCfg<3>::BN : v == 2 ? TileCfg<2>::BN : TileCfg<1>::BN;
     const long long tiles = (long long)((p.M + bm - 1) / bm) * ((p.N + bn - 1) / bn);
     int S = 1;
     if (variant >= 10) {
@@ -154,19 +163,20 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
 // the caller: ws == nullptr means no split).
 int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
     GemmParams p = p_in;
-    const int v = tile_variant(p, variant);
+    int v = tile_variant(p, variant);
     // Vector loads need 16-byte aligned bases, leading dims that are
     // multiples of 4 and contiguous extents that are multiples of 4.
     const int a_contig = (layout == kTN) ? p.M : p.K;
     const int b_contig = (layout == kNT) ? p.K : p.N;
     const bool vec = aligned16(p.A) && aligned16(p.B) && (p.lda % 4 == 0) &&
                      (p.ldb % 4 == 0) && (a_contig % 4 == 0) && (b_contig % 4 == 0);
-    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, v, vec, s);
+    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, v == 2 ? 1 : v, vec, s);
     if (mode != kCordic) return kErrUnsupported;
     if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
     p.k_inv = k_inv_of(p.iters);
     for (int i = 0; i < 24; ++i) p.coef[i] = gemm_coef(i);
-    const bool fixed = vec && layout != kTN;
+    const bool fixed = vec && layout != kTN && (p.iters == 8 || p.iters == 16 || p.iters == 24);
+    if (v == 2 && !fixed) v = 1;       // the 64x64 tile exists for the fixed-n kernels only
     if (fixed && p.iters == 8) return pick_fixed<8>(p, layout, v, s);
     if (fixed && p.iters == 16) return pick_fixed<16>(p, layout, v, s);
     if (fixed && p.iters == 24) return pick_fixed<24>(p, layout, v, s);

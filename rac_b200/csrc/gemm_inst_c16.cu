@@ -3,4 +3,5 @@
 namespace racb {
 RACB_GEMM_INST(kCordic, 16, kNN, 1, true) RACB_GEMM_INST(kCordic, 16, kNT, 1, true)
 RACB_GEMM_INST(kCordic, 16, kNN, 3, true) RACB_GEMM_INST(kCordic, 16, kNT, 3, true)
+RACB_GEMM_INST(kCordic, 16, kNN, 2, true) RACB_GEMM_INST(kCordic, 16, kNT, 2, true)
 }

@@ -3,4 +3,5 @@
 namespace racb {
 RACB_GEMM_INST(kCordic, 8, kNN, 1, true) RACB_GEMM_INST(kCordic, 8, kNT, 1, true)
 RACB_GEMM_INST(kCordic, 8, kNN, 3, true) RACB_GEMM_INST(kCordic, 8, kNT, 3, true)
+RACB_GEMM_INST(kCordic, 8, kNN, 2, true) RACB_GEMM_INST(kCordic, 8, kNT, 2, true)
 }

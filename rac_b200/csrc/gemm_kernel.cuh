@@ -95,8 +95,9 @@ struct TileLoader {
     }
 };
 
-template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC>
-__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC,
+          int MINB = 1>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN), MINB)
 k_gemm(const __grid_constant__ GemmParams p) {
     constexpr int TX = BN / TN, TY = BM / TM, NT = TX * TY;
     // Tiles are k-major in shared memory: row kk holds BM (BN) operands.
@@ -232,9 +233,12 @@ k_gemm(const __grid_constant__ GemmParams p) {
 // Tile variants.  1: 64x128 CTA tile, 8x8 per thread (the general case);
 // 3: 16x128, 4x4 per thread (M <= 32, e.g. decode-shaped rows).
 template <int V> struct TileCfg;
-template <> struct TileCfg<1> { static constexpr int BM = 64, BN = 128, BK = 8, TM = 8, TN = 8; };
-template <> struct TileCfg<2> { static constexpr int BM = 64, BN = 64, BK = 8, TM = 8, TN = 4; };
-template <> struct TileCfg<3> { static constexpr int BM = 16, BN = 128, BK = 8, TM = 4, TN = 4; };
+// 2: 64x64, 8x4 per thread, for mid-size problems whose 64x128 tiles would
+// leave resident slots empty (2048^3: 512 tiles for 592 slots).
+// MINB: resident CTAs per SM the register budget is sized for.
+template <> struct TileCfg<1> { static constexpr int BM = 64, BN = 128, BK = 8, TM = 8, TN = 8, MINB = 4; };
+template <> struct TileCfg<2> { static constexpr int BM = 64, BN = 64, BK = 8, TM = 8, TN = 4, MINB = 6; };
+template <> struct TileCfg<3> { static constexpr int BM = 16, BN = 128, BK = 8, TM = 4, TN = 4, MINB = 4; };
 
 template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
 int launch_inst(const GemmParams& p, cudaStream_t s) {
@@ -242,7 +246,7 @@ int launch_inst(const GemmParams& p, cudaStream_t s) {
     constexpr int NT = (T::BM / T::TM) * (T::BN / T::TN);
     dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN, p.ws ? p.splits : 1);
     if (grid.y > 65535) return kErrInvalidDim;
-    k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC><<<grid, NT, 0, s>>>(p);
+    k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC, T::MINB><<<grid, NT, 0, s>>>(p);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -57,6 +57,21 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         const int q = threadIdx.x + j * kRowThreads;
         v[j] = q < nq ? __ldcs(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    // gamma / beta are issued together with the row so that their (L2)
+    // latency overlaps the row's HBM latency instead of following the
+    // reductions.
+    float4 gv[OP == kRowSoftmax ? 1 : V], bv[OP == kRowLayer ? V : 1];
+    if constexpr (OP != kRowSoftmax) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int q = threadIdx.x + j * kRowThreads;
+            gv[j] = (gamma && q < nq) ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
+                                      : make_float4(1.f, 1.f, 1.f, 1.f);
+            if constexpr (OP == kRowLayer)
+                bv[j] = (beta && q < nq) ? __ldg(reinterpret_cast<const float4*>(beta) + q)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     const float fd = (float)d;
     if constexpr (OP == kRowSoftmax) {
         float m = -INFINITY;
@@ -93,12 +108,11 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         ss = block_reduce<false>(ss, red);
         const float ms = __fdiv_rn(ss, fd);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-        const float4* g4 = reinterpret_cast<const float4*>(gamma);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = gamma ? __ldg(g4 + q) : make_float4(1.f, 1.f, 1.f, 1.f);
+                const float4 g = gv[j];
                 __stcs(yr + q, make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), g.x),
                                            __fmul_rn(__fmul_rn(v[j].y, inv), g.y),
                                            __fmul_rn(__fmul_rn(v[j].z, inv), g.z),
@@ -126,14 +140,12 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         var = block_reduce<false>(var, red);
         var = __fdiv_rn(var, fd);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        const float4* g4 = reinterpret_cast<const float4*>(gamma);
-        const float4* b4 = reinterpret_cast<const float4*>(beta);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = gamma ? __ldg(g4 + q) : make_float4(1.f, 1.f, 1.f, 1.f);
-                const float4 b = beta ? __ldg(b4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 g = gv[j];
+                const float4 b = bv[j];
                 __stcs(yr + q, make_float4(
                     __fmaf_rn(g.x, __fmul_rn(__fsub_rn(v[j].x, mean), inv), b.x),
                     __fmaf_rn(g.y, __fmul_rn(__fsub_rn(v[j].y, mean), inv), b.y),

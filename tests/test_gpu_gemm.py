@@ -153,7 +153,7 @@ def test_cordic_equals_fast_on_rotated_operand(cuda):
 
 def test_splitk_skinny_config(cuda, orc):
     """The BASELINE skinny shape M=16, N=11008, K=4096 runs split-K (86 output
-    tiles on 148 SMs): normwise <= 1e-5 to the sequential restatement,
+    tiles on 148 SMs): normwise <= 1e-4 to the sequential restatement,
     deterministic across calls."""
     M, N, K = 16, 11008, 4096
     rng = np.random.default_rng(16)
@@ -164,7 +164,7 @@ def test_splitk_skinny_config(cuda, orc):
     C2 = ext.gemm(dA, dB, LAYOUT_NN, 16, 1)
     assert torch.equal(C1, C2)
     want = orc.gemm(A, B, "nn", 1, 16)
-    assert _normwise(C1.cpu().numpy(), want) <= 1e-5
+    assert _normwise(C1.cpu().numpy(), want) <= NORM_TOL
     C3 = ext.gemm(dA, dB, LAYOUT_NN, 16, 1, variant=3)      # no split
     assert np.array_equal(C3.cpu().numpy(), want)
 
@@ -178,4 +178,4 @@ def test_splitk_forced_with_epilogue(cuda, orc, layout):
     kw = dict(bias=_t(bias, cuda), act=3, residual=_t(R, cuda))
     ref = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=1, **kw).cpu().numpy()
     got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=13, **kw).cpu().numpy()
-    assert _normwise(got, ref) <= 1e-5
+    assert _normwise(got, ref) <= NORM_TOL
