@@ -127,11 +127,21 @@ __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
 
 // _cordic_rotate of lib/c/rac_cpu.c:90-118: wrap theta to (-pi, pi], fold
 // into [-pi/2, pi/2] by negating (x, y), then ITERS micro-rotations whose
-// direction is the sign of the residual angle.  (x, y) arrive pre-scaled.
-// The direction is read from the angle's sign bit: the residual can only be
-// -0 at entry (x - y == 0 rounds to +0 afterwards), which the +0.0f add
-// removes, and a NaN angle takes the comparison path to keep d = -1.
-// Returns false when the wrap loop hit kWrapLimit.
+// direction d_i = (angle_i >= 0) ? +1 : -1 is the sign of the residual angle.
+// (x, y) arrive pre-scaled.  Returns false when the wrap loop hit kWrapLimit.
+//
+// Pipe balance: the direction of iterations i >= 1 is computed on the FMA
+// pipe, not with sign-bit logic on the (half-rate) ALU pipe:
+//   t_i = sat(angle_i * 2^126 + 1)          -> 1 if angle_i >= 0 (incl. -0),
+//                                              0 if angle_i < 0 or NaN
+//   d_i * 2^-i   = t_i * 2^(1-i) - 2^-i     (exact: t_i is 0 or 1)
+//   d_i * atan_i = t_i * 2 atan_i - atan_i  (exact)
+// This equals the comparison whenever angle_i is 0 or |angle_i| >= 2^-125.
+// For i >= 1 that always holds: angle_1 = fl(angle_0 -+ atan_0) has
+// magnitude >= 2^-2 or is a difference of floats near atan_0 (a multiple of
+// 2^-25), and every later angle is a rounded sum of it and table entries,
+// hence 0 or a multiple of 2^-48.  Iteration 0 (arbitrary input angle,
+// possibly subnormal) uses the comparison itself.
 template <int ITERS>
 __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta) {
     const float TAU = 2.0f * kPi;
@@ -145,28 +155,23 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta)
     } else if (theta < -kPi * 0.5f) {
         x = -x; y = -y; theta = __fadd_rn(theta, kPi);
     }
-    if (theta != theta) {
-        // NaN residual: every comparison is false, so d = -1 throughout.
-        float s = 1.0f;
+    float angle = theta;
+    {   // iteration 0: scale 1
+        const float d = (angle >= 0.0f) ? 1.0f : -1.0f;
+        const float xn = __fmaf_rn(-d, y, x);
+        y = __fmaf_rn(d, x, y);
+        x = xn;
+        if (ITERS > 1) angle = __fsub_rn(angle, d * atan_entry(0));
+    }
 #pragma unroll
-        for (int i = 0; i < ITERS; ++i) {
-            const float xn = __fmaf_rn(s, y, x);
-            y = __fmaf_rn(-s, x, y);
-            x = xn;
-            s *= 0.5f;
-        }
-    } else {
-        float angle = __fadd_rn(theta, 0.0f);   // -0 -> +0
-#pragma unroll
-        for (int i = 0; i < ITERS; ++i) {
-            const uint32_t sgn = __float_as_uint(angle) & 0x80000000u;
-            const float ds = __uint_as_float(__float_as_uint(pow2neg(i)) ^ sgn);
-            const float xn = __fmaf_rn(-ds, y, x);
-            y = __fmaf_rn(ds, x, y);
-            x = xn;
-            if (i + 1 < ITERS)
-                angle = __fsub_rn(angle, __uint_as_float(__float_as_uint(atan_entry(i)) ^ sgn));
-        }
+    for (int i = 1; i < ITERS; ++i) {
+        const float t = __saturatef(__fmaf_rn(angle, 0x1p126f, 1.0f));
+        const float ds = __fmaf_rn(t, 2.0f * pow2neg(i), -pow2neg(i));
+        const float xn = __fmaf_rn(-ds, y, x);
+        y = __fmaf_rn(ds, x, y);
+        x = xn;
+        if (i + 1 < ITERS)
+            angle = __fsub_rn(angle, __fmaf_rn(t, 2.0f * atan_entry(i), -atan_entry(i)));
     }
     xr = x; yr = y;
     return ok;

@@ -45,21 +45,12 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
                                                          float* __restrict__ y,
                                                          const float* __restrict__ gamma,
                                                          const float* __restrict__ beta,
-                                                         float eps, int d) {
+                                                         float eps, int d, long long rows) {
     __shared__ float red[kRowWarps];
-    const long long row = blockIdx.x;
-    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
-    float4* yr = reinterpret_cast<float4*>(y + row * d);
     const int nq = d / 4;
-    float4 v[V];
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-        const int q = threadIdx.x + j * kRowThreads;
-        v[j] = q < nq ? __ldcs(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    // gamma / beta are issued together with the row so that their (L2)
-    // latency overlaps the row's HBM latency instead of following the
-    // reductions.
+    // Persistent CTAs: gamma / beta are loaded once per CTA into registers
+    // and reused for every row the CTA handles (one L2 read per CTA instead
+    // of one per row).
     float4 gv[OP == kRowSoftmax ? 1 : V], bv[OP == kRowLayer ? V : 1];
     if constexpr (OP != kRowSoftmax) {
 #pragma unroll
@@ -73,6 +64,15 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         }
     }
     const float fd = (float)d;
+    for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
+    float4* yr = reinterpret_cast<float4*>(y + row * d);
+    float4 v[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int q = threadIdx.x + j * kRowThreads;
+        v[j] = q < nq ? __ldcs(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if constexpr (OP == kRowSoftmax) {
         float m = -INFINITY;
 #pragma unroll
@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
             }
         }
     }
+    }  // rows
 }
 
 // Any d, any alignment: reductions stream the row from global memory.
@@ -204,6 +205,23 @@ __global__ void __launch_bounds__(kRowThreads) k_row_any(const float* __restrict
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Grid = resident CTAs per SM x SMs (persistent), capped at the row count.
+template <int OP, int V>
+static void launch_vec(const float* x, float* y, const float* g, const float* b, float eps,
+                       int d, long long rows, cudaStream_t s) {
+    static int per_sm = 0, sms = 0;
+    if (!per_sm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_row_vec<OP, V>, kRowThreads, 0);
+        if (per_sm < 1) per_sm = 1;
+    }
+    long long grid = (long long)per_sm * sms;
+    if (grid > rows) grid = rows;
+    k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d, rows);
+}
+
 template <int OP>
 static int launch_rows(const float* x, float* y, const float* g, const float* b, float eps,
                        long long rows, int d, cudaStream_t s) {
@@ -213,13 +231,12 @@ static int launch_rows(const float* x, float* y, const float* g, const float* b,
     if (rows > 0x7fffffffLL) return kErrInvalidDim;
     const bool vec = (d % 4 == 0) && al16(x) && al16(y) && (!g || al16(g)) && (!b || al16(b));
     const int nq = d / 4;
-    const dim3 grid((unsigned)rows);
-    if (vec && nq <= kRowThreads * 1) k_row_vec<OP, 1><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
-    else if (vec && nq <= kRowThreads * 2) k_row_vec<OP, 2><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
-    else if (vec && nq <= kRowThreads * 4) k_row_vec<OP, 4><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
-    else if (vec && nq <= kRowThreads * 8) k_row_vec<OP, 8><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
-    else if (vec && nq <= kRowThreads * 16) k_row_vec<OP, 16><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
-    else k_row_any<OP><<<grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d);
+    if (vec && nq <= kRowThreads * 1) launch_vec<OP, 1>(x, y, g, b, eps, d, rows, s);
+    else if (vec && nq <= kRowThreads * 2) launch_vec<OP, 2>(x, y, g, b, eps, d, rows, s);
+    else if (vec && nq <= kRowThreads * 4) launch_vec<OP, 4>(x, y, g, b, eps, d, rows, s);
+    else if (vec && nq <= kRowThreads * 8) launch_vec<OP, 8>(x, y, g, b, eps, d, rows, s);
+    else if (vec && nq <= kRowThreads * 16) launch_vec<OP, 16>(x, y, g, b, eps, d, rows, s);
+    else k_row_any<OP><<<dim3((unsigned)rows), kRowThreads, 0, s>>>(x, y, g, b, eps, d);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -199,3 +199,26 @@ def test_norms_golden_host_abi(cuda, golden):
     m = xd.mean(1, keepdims=True)
     exact = g * (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
     assert O.reduction_ok(y, golden["ln_out"], exact)
+
+
+@pytest.mark.parametrize("it", [4, 7, 8, 16, 24])
+def test_rotate_direction_edge_angles(cuda, orc, it):
+    """Angles whose residuals hit exactly 0, tiny or subnormal values, NaN:
+    the direction logic must reproduce `angle >= 0` of lib/c bit for bit."""
+    atan = np.array([0.78539816, 0.46364761, 0.24497866, 0.12435499, 0.06241881,
+                     0.03123983, 0.01562373, 0.00781234], np.float32)
+    partial = [np.float32(0.0)]
+    for s in ([1, 1], [1, -1], [1, 1, 1], [1, -1, 1, -1], [1, 1, -1, 1, -1, 1]):
+        acc = np.float32(0.0)
+        for i, sg in enumerate(s):
+            acc = np.float32(acc + np.float32(sg) * atan[i])
+        partial.append(acc)
+    th = np.array(partial + [-p for p in partial] +
+                  [1e-40, -1e-40, 1.4e-45, -1.4e-45, 1e-30, -1e-30, np.nan, -np.nan,
+                   atan[0], -atan[0], np.float32(np.pi / 2), -np.float32(np.pi / 2)], np.float32)
+    rng = np.random.default_rng(it)
+    v = rng.standard_normal((th.size, 2)).astype(np.float32)
+    got = ext.rotate_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
+    assert _bits_equal(got, orc.rotate_batch(v, th, it, False))
+    got = ext.project_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
+    assert _bits_equal(got, orc.project_batch(v, th, it))
