@@ -399,7 +399,7 @@ def run_stream(args, world, rank, local) -> dict | None:
         bytes_, units, unit_name = 8 * x.numel(), x.numel(), "Gelem/s"
         cfg = "rac_softmax [32768, 4096] fp32 ~N(0,9)"
     else:
-        x = torch.randn((16384, 4096), device=dev, generator=g)
+        x = torch.randn((args.rows, 4096), device=dev, generator=g)
         gam = torch.rand(4096, device=dev, generator=g) + 0.5
         bet = torch.randn(4096, device=dev, generator=g) * 0.1
         if w == "rmsnorm":
@@ -407,7 +407,7 @@ def run_stream(args, world, rank, local) -> dict | None:
         else:
             fn = lambda: ext.layernorm(x, gam, bet, 1e-6)         # noqa: E731
         bytes_, units, unit_name = 8 * x.numel(), x.numel(), "Gelem/s"
-        cfg = f"rac_{w} [16384, 4096] fp32, eps 1e-6"
+        cfg = f"rac_{w} [{args.rows}, 4096] fp32, eps 1e-6"
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
@@ -462,6 +462,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=16)
     ap.add_argument("--mode", choices=["cordic", "fast"], default="cordic")
     ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--rows", type=int, default=16384, help="norm workloads: row count")
     ap.add_argument("--log2n", type=int, default=26, help="rotate workload: log2 of the vector count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

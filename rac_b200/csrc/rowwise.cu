@@ -48,31 +48,38 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
                                                          float eps, int d, long long rows) {
     __shared__ float red[kRowWarps];
     const int nq = d / 4;
-    // Persistent CTAs: gamma / beta are loaded once per CTA into registers
-    // and reused for every row the CTA handles (one L2 read per CTA instead
-    // of one per row).
-    float4 gv[OP == kRowSoftmax ? 1 : V], bv[OP == kRowLayer ? V : 1];
+    // Persistent CTAs.  gamma / beta are staged once per CTA into shared
+    // memory (one L2 read per CTA, not per row), and the next row's loads are
+    // issued before the current row is reduced, so every CTA keeps one row of
+    // HBM reads in flight while it computes.
+    extern __shared__ float4 s_gb[];     // [nq] gamma, then [nq] beta
     if constexpr (OP != kRowSoftmax) {
+        for (int q = threadIdx.x; q < nq; q += kRowThreads) {
+            s_gb[q] = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
+                            : make_float4(1.f, 1.f, 1.f, 1.f);
+            if constexpr (OP == kRowLayer)
+                s_gb[nq + q] = beta ? __ldg(reinterpret_cast<const float4*>(beta) + q)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        __syncthreads();
+    }
+    const float fd = (float)d;
+    float4 nxt[V];
+    auto load_row = [&](long long r) {
+        const float4* xr = reinterpret_cast<const float4*>(x + r * d);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
-            gv[j] = (gamma && q < nq) ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
-                                      : make_float4(1.f, 1.f, 1.f, 1.f);
-            if constexpr (OP == kRowLayer)
-                bv[j] = (beta && q < nq) ? __ldg(reinterpret_cast<const float4*>(beta) + q)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            nxt[j] = (r < rows && q < nq) ? __ldcs(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    }
-    const float fd = (float)d;
+    };
+    load_row(blockIdx.x);
     for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
-    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
     float4* yr = reinterpret_cast<float4*>(y + row * d);
     float4 v[V];
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-        const int q = threadIdx.x + j * kRowThreads;
-        v[j] = q < nq ? __ldcs(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int j = 0; j < V; ++j) v[j] = nxt[j];
+    load_row(row + gridDim.x);           // in flight during this row's reductions
     if constexpr (OP == kRowSoftmax) {
         float m = -INFINITY;
 #pragma unroll
@@ -112,7 +119,7 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = gv[j];
+                const float4 g = s_gb[q];
                 __stcs(yr + q, make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), g.x),
                                            __fmul_rn(__fmul_rn(v[j].y, inv), g.y),
                                            __fmul_rn(__fmul_rn(v[j].z, inv), g.z),
@@ -144,8 +151,8 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = gv[j];
-                const float4 b = bv[j];
+                const float4 g = s_gb[q];
+                const float4 b = s_gb[nq + q];
                 __stcs(yr + q, make_float4(
                     __fmaf_rn(g.x, __fmul_rn(__fsub_rn(v[j].x, mean), inv), b.x),
                     __fmaf_rn(g.y, __fmul_rn(__fsub_rn(v[j].y, mean), inv), b.y),
@@ -209,17 +216,18 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 template <int OP, int V>
 static void launch_vec(const float* x, float* y, const float* g, const float* b, float eps,
                        int d, long long rows, cudaStream_t s) {
-    static int per_sm = 0, sms = 0;
-    if (!per_sm) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_row_vec<OP, V>, kRowThreads, 0);
-        if (per_sm < 1) per_sm = 1;
-    }
+    const int nq = d / 4;
+    const size_t smem = OP == kRowSoftmax ? 0 : (OP == kRowLayer ? 2 : 1) * sizeof(float4) * nq;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(k_row_vec<OP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_row_vec<OP, V>, kRowThreads, smem);
+    if (per_sm < 1) per_sm = 1;
     long long grid = (long long)per_sm * sms;
     if (grid > rows) grid = rows;
-    k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d, rows);
+    k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, smem, s>>>(x, y, g, b, eps, d, rows);
 }
 
 template <int OP>

@@ -57,10 +57,21 @@ __global__ void __launch_bounds__(256) k_rotate(const float2* __restrict__ v,
     long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (vec) {
         const long long nq = n / 4;
+        // Software pipeline: the next quad's 48 bytes are requested before the
+        // current quad's rotations run.
+        float4 v01n = make_float4(0.f, 0.f, 0.f, 0.f), v23n = v01n, tn = v01n;
+        if (i0 < nq) {
+            v01n = __ldcs(reinterpret_cast<const float4*>(v) + 2 * i0);
+            v23n = __ldcs(reinterpret_cast<const float4*>(v) + 2 * i0 + 1);
+            tn = __ldcs(reinterpret_cast<const float4*>(th) + i0);
+        }
         for (long long q = i0; q < nq; q += stride) {
-            const float4 v01 = __ldcs(reinterpret_cast<const float4*>(v) + 2 * q);
-            const float4 v23 = __ldcs(reinterpret_cast<const float4*>(v) + 2 * q + 1);
-            const float4 t = __ldcs(reinterpret_cast<const float4*>(th) + q);
+            const float4 v01 = v01n, v23 = v23n, t = tn;
+            if (q + stride < nq) {
+                v01n = __ldcs(reinterpret_cast<const float4*>(v) + 2 * (q + stride));
+                v23n = __ldcs(reinterpret_cast<const float4*>(v) + 2 * (q + stride) + 1);
+                tn = __ldcs(reinterpret_cast<const float4*>(th) + q + stride);
+            }
             float x0 = __fmul_rn(v01.x, k_inv), y0 = __fmul_rn(v01.y, k_inv);
             float x1 = __fmul_rn(v01.z, k_inv), y1 = __fmul_rn(v01.w, k_inv);
             float x2 = __fmul_rn(v23.x, k_inv), y2 = __fmul_rn(v23.y, k_inv);
