@@ -383,7 +383,8 @@ def run_stream(args, world, rank, local) -> dict | None:
         n = 1 << args.log2n
         v = torch.randn((n, 2), device=dev, generator=g)
         th = (torch.rand(n, device=dev, generator=g) * 2 - 1) * 3.14159265
-        fn = lambda: ext.rotate_batch(v, th, args.iters)          # noqa: E731
+        ro = torch.empty_like(v)
+        fn = lambda: ext.rotate_batch(v, th, args.iters, out=ro)  # noqa: E731
         bytes_, units, unit_name = 20 * n, n, "Gvec/s"
         cfg = f"rac_rotate_batch_n 2^{args.log2n} float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
     elif w == "rope":
@@ -402,10 +403,11 @@ def run_stream(args, world, rank, local) -> dict | None:
         x = torch.randn((args.rows, 4096), device=dev, generator=g)
         gam = torch.rand(4096, device=dev, generator=g) + 0.5
         bet = torch.randn(4096, device=dev, generator=g) * 0.1
+        y = torch.empty_like(x)
         if w == "rmsnorm":
-            fn = lambda: ext.rmsnorm(x, gam, 1e-6)                # noqa: E731
+            fn = lambda: ext.rmsnorm(x, gam, 1e-6, out=y)         # noqa: E731
         else:
-            fn = lambda: ext.layernorm(x, gam, bet, 1e-6)         # noqa: E731
+            fn = lambda: ext.layernorm(x, gam, bet, 1e-6, out=y)  # noqa: E731
         bytes_, units, unit_name = 8 * x.numel(), x.numel(), "Gelem/s"
         cfg = f"rac_{w} [{args.rows}, 4096] fp32, eps 1e-6"
     for _ in range(args.warmup):

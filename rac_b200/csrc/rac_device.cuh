@@ -142,6 +142,14 @@ __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
 // 2^-25), and every later angle is a rounded sum of it and table entries,
 // hence 0 or a multiple of 2^-48.  Iteration 0 (arbitrary input angle,
 // possibly subnormal) uses the comparison itself.
+// sat(a * b + c) as one FFMA.SAT (PTX fma.rn.sat.f32: result clamped to
+// [0, 1], NaN -> +0).
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+    float r;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 template <int ITERS>
 __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta) {
     const float TAU = 2.0f * kPi;
@@ -165,7 +173,7 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta)
     }
 #pragma unroll
     for (int i = 1; i < ITERS; ++i) {
-        const float t = __saturatef(__fmaf_rn(angle, 0x1p126f, 1.0f));
+        const float t = fma_sat(angle, 0x1p126f, 1.0f);
         const float ds = __fmaf_rn(t, 2.0f * pow2neg(i), -pow2neg(i));
         const float xn = __fmaf_rn(-ds, y, x);
         y = __fmaf_rn(ds, x, y);

@@ -218,13 +218,20 @@ static void launch_vec(const float* x, float* y, const float* g, const float* b,
                        int d, long long rows, cudaStream_t s) {
     const int nq = d / 4;
     const size_t smem = OP == kRowSoftmax ? 0 : (OP == kRowLayer ? 2 : 1) * sizeof(float4) * nq;
-    int dev = 0, sms = 148, per_sm = 1;
+    // Occupancy depends on (device, smem bytes); cache the last answer per device.
+    static thread_local int c_dev = -1, c_sms = 0, c_per = 0;
+    static thread_local size_t c_smem = ~size_t(0);
+    int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(k_row_vec<OP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_row_vec<OP, V>, kRowThreads, smem);
-    if (per_sm < 1) per_sm = 1;
+    if (dev != c_dev || smem != c_smem) {
+        cudaDeviceGetAttribute(&c_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(k_row_vec<OP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c_per, k_row_vec<OP, V>, kRowThreads, smem);
+        if (c_per < 1) c_per = 1;
+        c_dev = dev; c_smem = smem;
+    }
+    const int sms = c_sms, per_sm = c_per;
     long long grid = (long long)per_sm * sms;
     if (grid > rows) grid = rows;
     k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, smem, s>>>(x, y, g, b, eps, d, rows);

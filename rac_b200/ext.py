@@ -215,13 +215,14 @@ def _prep(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous()
 
 
-def rotate_batch(v: torch.Tensor, theta: torch.Tensor, iters: int | None = None) -> torch.Tensor:
+def rotate_batch(v: torch.Tensor, theta: torch.Tensor, iters: int | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
     """v[..., 2] rotated by theta[...]: rac_rotate_batch (iters None: literal
     RAC_K_INV, 16 iterations, lib/c/rac_cpu.c:136-139) or rac_rotate_n."""
     v, theta = _prep(v), _prep(theta)
     if v.shape[-1] != 2 or v.numel() != 2 * theta.numel():
         raise ValueError("v must be [..., 2] with one angle per vector")
-    out = torch.empty_like(v)
+    out = torch.empty_like(v) if out is None else out
     lit = 1 if iters is None else 0
     with torch.cuda.device(v.device):
         _lib.call("rac_rotate_batch_async", v.data_ptr(), theta.data_ptr(), out.data_ptr(),
@@ -286,11 +287,12 @@ def softmax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     return y
 
 
-def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-6,
+            out: torch.Tensor | None = None) -> torch.Tensor:
     """lib/c/rac_cpu.c:548-574 over the last dim."""
     x = _prep(x)
     g = _prep(gamma) if gamma is not None else None
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     d = x.shape[-1]
     with torch.cuda.device(x.device):
         _lib.call("rac_rmsnorm_async", x.data_ptr(), y.data_ptr(), _ptr(g), float(eps),
@@ -298,12 +300,13 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-
     return y
 
 
-def layernorm(x, gamma=None, beta=None, eps: float = 1e-5) -> torch.Tensor:
+def layernorm(x, gamma=None, beta=None, eps: float = 1e-5,
+              out: torch.Tensor | None = None) -> torch.Tensor:
     """lib/c/rac_cpu.c:507-546 over the last dim."""
     x = _prep(x)
     g = _prep(gamma) if gamma is not None else None
     b = _prep(beta) if beta is not None else None
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     d = x.shape[-1]
     with torch.cuda.device(x.device):
         _lib.call("rac_layernorm_async", x.data_ptr(), y.data_ptr(), _ptr(g), _ptr(b), float(eps),
