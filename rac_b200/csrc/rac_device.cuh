@@ -134,8 +134,7 @@ __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
 // pipe, not with sign-bit logic on the (half-rate) ALU pipe:
 //   t_i = sat(angle_i * 2^126 + 1)          -> 1 if angle_i >= 0 (incl. -0),
 //                                              0 if angle_i < 0 or NaN
-//   d_i * 2^-i   = t_i * 2^(1-i) - 2^-i     (exact: t_i is 0 or 1)
-//   d_i * atan_i = t_i * 2 atan_i - atan_i  (exact)
+//   d_i = 2 t_i - 1,  d_i * 2^-i and d_i * atan_i exact (d_i = +-1)
 // This equals the comparison whenever angle_i is 0 or |angle_i| >= 2^-125.
 // For i >= 1 that always holds: angle_1 = fl(angle_0 -+ atan_0) has
 // magnitude >= 2^-2 or is a difference of floats near atan_0 (a multiple of
@@ -171,15 +170,20 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta)
         x = xn;
         if (ITERS > 1) angle = __fsub_rn(angle, d * atan_entry(0));
     }
+    // Each instruction below carries at most one immediate (FFMA encodes one);
+    // the +1 / -1 addends live in registers, so an iteration is exactly six
+    // FMA-pipe instructions with no constant materialisation.
+    const float one = 1.0f, neg_one = -1.0f;
 #pragma unroll
     for (int i = 1; i < ITERS; ++i) {
-        const float t = fma_sat(angle, 0x1p126f, 1.0f);
-        const float ds = __fmaf_rn(t, 2.0f * pow2neg(i), -pow2neg(i));
+        const float t = fma_sat(angle, 0x1p126f, one);     // 1: angle >= 0, 0: < 0 / NaN
+        const float e = __fmaf_rn(t, 2.0f, neg_one);       // d_i = +-1
+        const float ds = __fmul_rn(e, pow2neg(i));          // d_i * 2^-i (exact)
         const float xn = __fmaf_rn(-ds, y, x);
         y = __fmaf_rn(ds, x, y);
         x = xn;
         if (i + 1 < ITERS)
-            angle = __fsub_rn(angle, __fmaf_rn(t, 2.0f * atan_entry(i), -atan_entry(i)));
+            angle = __fmaf_rn(-e, atan_entry(i), angle);    // angle - d_i*atan_i, one rounding
     }
     xr = x; yr = y;
     return ok;
