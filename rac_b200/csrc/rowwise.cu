@@ -232,8 +232,11 @@ static void launch_vec(const float* x, float* y, const float* g, const float* b,
         c_dev = dev; c_smem = smem;
     }
     const int sms = c_sms, per_sm = c_per;
-    long long grid = (long long)per_sm * sms;
+    // Softmax has no per-CTA state worth amortising: one CTA per row lets the
+    // hardware overlap rows across CTAs (measured faster than persistent).
+    long long grid = OP == kRowSoftmax ? rows : (long long)per_sm * sms;
     if (grid > rows) grid = rows;
+    if (grid > 0x7fffffffLL) grid = 0x7fffffffLL;
     k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, smem, s>>>(x, y, g, b, eps, d, rows);
 }
 
