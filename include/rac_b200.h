@@ -109,6 +109,25 @@ int rac_gemm_async(const float *A, long long lda, const float *B, long long ldb,
                    int iters, float alpha, float beta, int act, int variant,
                    void *stream);
 
+/* rac_gemm_async for callers that cannot allocate device memory -- no
+ * counterpart in the reference.  Same arguments and result as
+ * rac_gemm_async, always split-K (`splits` K chunks; 0 = the automatic
+ * count, at least 1), with the partial sums held in a 16 MiB array compiled
+ * into the library instead of a workspace allocated per call: the call makes
+ * no allocation at all.  Hosts that give a library a fixed device-memory
+ * budget, or cannot tolerate an allocation on a latency-critical path, use
+ * this form.  Limits: splits * M * N <= 4 Mi floats (else
+ * RAC_ERR_INVALID_DIM with the sizes in rac_last_error_string()); every GPU
+ * that loads the library holds the 16 MiB until exit; all calls share the
+ * array, so calls whose kernels overlap on the GPU (two streams, two host
+ * threads) race.  The first call on a device looks the array's address up
+ * (make it before any stream capture on that device). */
+int rac_gemm_splitk_noalloc_async(const float *A, long long lda, const float *B, long long ldb,
+                                  float *C, long long ldc, const float *Cin, long long ldcin,
+                                  const float *bias, int M, int N, int K, int layout, int mode,
+                                  int iters, float alpha, float beta, int act, int splits,
+                                  void *stream);
+
 int rac_rotate_batch_async(const float2 *v, const float *theta, float2 *out, long long n,
                            int iters, int literal_kinv, void *stream);
 int rac_project_batch_async(const float2 *v, const float *theta, float *out, long long n,

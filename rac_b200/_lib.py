@@ -87,6 +87,8 @@ _SIGS = {
     "rac_launch_tn": (None, [_vp, _vp, _vp, _i, _i, _i, _f, _f, _vp]),
     "rac_gemm_async": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _vp, _i, _i, _i,
                             _i, _i, _i, _f, _f, _i, _i, _vp]),
+    "rac_gemm_splitk_noalloc_async": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _vp, _i, _i,
+                                           _i, _i, _i, _i, _f, _f, _i, _i, _vp]),
     "rac_rotate_batch_async": (_i, [_vp, _vp, _vp, _ll, _i, _i, _vp]),
     "rac_project_batch_async": (_i, [_vp, _vp, _vp, _ll, _i, _vp]),
     "rac_sincos_batch_async": (_i, [_vp, _vp, _vp, _ll, _vp]),

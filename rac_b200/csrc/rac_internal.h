@@ -64,6 +64,9 @@ int launch_gemm(const GemmParams& p, int layout, int mode, int variant,
 // re-mapped on every call.  Idempotent, once per device.
 void keep_device_pool();
 
+// Records `st` as this thread's rac_last_error() with message `msg`.
+int record_status(int st, const char* msg);
+
 // Per-device error word that bounded device loops set (see rac_device.cuh).
 unsigned int* device_error_word(int device);
 

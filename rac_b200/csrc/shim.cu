@@ -146,6 +146,16 @@ struct Call {
 
 }  // namespace
 
+namespace racb {
+// Lets other translation units of the library record a status with their
+// own message (see rac_internal.h).
+int record_status(int st, const char* msg) {
+    t_status = st;
+    std::snprintf(t_msg, sizeof t_msg, "%s", msg ? msg : (st ? "error" : "ok"));
+    return st;
+}
+}  // namespace racb
+
 // ── 1. errors and knobs ─────────────────────────────────────────────────
 
 RAC_API int rac_last_error(void) { return t_status; }
