@@ -153,7 +153,7 @@ def cpu_matmul_baseline(M: int, N: int, K: int, iters: int, reps: int = 1, warm:
     A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
     cores = os.cpu_count() or 1
-    out = {"cores": int(os.environ.get("OMP_NUM_THREADS", cores))}
+    out = {"cores": cores}
     if O.ref_available():
         for _ in range(warm):
             O.ref_sgemm(A, B)
@@ -228,9 +228,12 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     M = N = K = 4096
+    cores = os.cpu_count() or 1
+    # torchrun sets OMP_NUM_THREADS=1 per process; the reference arm uses every
+    # host thread (OpenMP reads the variable when the library is loaded).
+    os.environ["OMP_NUM_THREADS"] = str(cores)
     import numpy as np
     import oracle as O
-    cores = os.cpu_count() or 1
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/librac_ref.so not built"}))
         return
@@ -451,6 +454,12 @@ def run_stream(args, world, rank, local) -> dict | None:
     }
 
 
+def _all_host_threads() -> None:
+    """The CPU baselines use every host core; set before oracle/ is loaded."""
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -473,6 +482,7 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
+    _all_host_threads()
     world, rank, local = dist_init()
     if args.workload == "matmul":
         out = run_matmul(args, world, rank, local)

@@ -132,6 +132,10 @@ def check(status: int | None = None) -> None:
         raise RacError(st, L.rac_last_error_string().decode())
 
 
+CALLS = {"n": 0}     # entry-point calls made through call(); the bench reports it
+
+
 def call(name: str, *args) -> None:
     """Calls an int-returning entry point and raises on a non-zero status."""
+    CALLS["n"] += 1
     check(getattr(lib(), name)(*args))
