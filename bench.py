@@ -365,11 +365,12 @@ def run_matmul(args, world, rank, local) -> dict | None:
 
 
 def _splits(M: int, N: int, K: int, sms: int) -> int:
-    """Mirror of the library's split-K rule (gemm_dispatch.cu splitk_count)."""
-    bm, bn = (16, 128) if M <= 32 else (64, 128)
-    tiles = -(-M // bm) * -(-N // bn)
-    if M > 32 and tiles < 8 * sms:
-        tiles = -(-M // 64) * -(-N // 64)            # 64x64 tiles
+    """Mirror of the library's tile and split-K rules (gemm_dispatch.cu)."""
+    if M <= 32:
+        tiles = -(-M // 16) * -(-N // 128)
+    else:
+        cands = [(-(-M // bm) * -(-N // bn), bm * bn) for bm, bn in ((64, 128), (64, 64), (32, 64))]
+        tiles = min(cands, key=lambda c: (-(-c[0] // sms)) * c[1])[0]
     if tiles >= sms or K < 1024:
         return 1
     return max(1, min(-(-4 * sms // tiles), K // 256))

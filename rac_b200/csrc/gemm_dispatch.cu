@@ -13,7 +13,8 @@ E4(kCordic, 0, kNN) E4(kCordic, 0, kNT) E4(kCordic, 0, kTN)
 #define E2(ITERS) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 1, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 1, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 3, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 3, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 2, true) \
-    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 2, true)
+    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 2, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 4, true) \
+    RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 4, true)
 E2(8) E2(16) E2(24)
 
 template <int MODE, int ITERS, int LAYOUT>
@@ -38,6 +39,8 @@ template <int ITERS>
 static int pick_fixed(const GemmParams& p, int layout, int v, cudaStream_t s) {
     if (v == 2) return layout == kNN ? launch_inst<kCordic, ITERS, kNN, 2, true>(p, s)
                                      : launch_inst<kCordic, ITERS, kNT, 2, true>(p, s);
+    if (v == 4) return layout == kNN ? launch_inst<kCordic, ITERS, kNN, 4, true>(p, s)
+                                     : launch_inst<kCordic, ITERS, kNT, 4, true>(p, s);
     if (layout == kNN) return pick_tile<kCordic, ITERS, kNN>(p, v, true, s);
     return pick_tile<kCordic, ITERS, kNT>(p, v, true, s);
 }
@@ -73,13 +76,23 @@ void keep_device_pool() {
 
 static int sm_count();
 
-// 3 for M <= 32; 2 when 64x128 tiles would fill fewer than two rounds of the
-// resident slots (4 per SM); 1 otherwise.  Variants 1-3 can be forced.
+// 3 for M <= 32.  Otherwise the tile (64x128, 64x64 or 32x64) that minimises
+// the work of the most loaded SM, ceil(tiles / SMs) x tile area -- the GEMM is
+// issue-bound per SM, so that is its run time; ties go to the larger tile.
+// Variants 1-4 can be forced.
 static int tile_variant(const GemmParams& p, int variant) {
-    if (variant >= 1 && variant <= 3) return variant;
+    if (variant >= 1 && variant <= 4) return variant;
     if (p.M <= 32) return 3;
-    const long long tiles = (long long)((p.M + 63) / 64) * ((p.N + 127) / 128);
-    return tiles < 8LL * sm_count() ? 2 : 1;
+    const long long sms = sm_count();
+    const int bms[3] = {64, 64, 32}, bns[3] = {128, 64, 64}, vs[3] = {1, 2, 4};
+    int best = 1;
+    long long best_cost = -1;
+    for (int i = 0; i < 3; ++i) {
+        const long long tiles = (long long)((p.M + bms[i] - 1) / bms[i]) * ((p.N + bns[i] - 1) / bns[i]);
+        const long long cost = (tiles + sms - 1) / sms * bms[i] * bns[i];
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = vs[i]; }
+    }
+    return best;
 }
 
 // Split-K when the output tiles cannot fill the machine: fewer tiles than
@@ -88,8 +101,8 @@ static int tile_variant(const GemmParams& p, int variant) {
 int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
     (void)layout; (void)mode;
     const int v = tile_variant(p, variant);
-    const int bm = v == 3 ? TileCfg<3>::BM : TileCfg<1>::BM;
-    const int bn = v == 3 ? TileCfg<3>::BN : v == 2 ? TileCfg<2>::BN : TileCfg<1>::BN;
+    const int bm = v == 3 ? TileCfg<3>::BM : v == 4 ? TileCfg<4>::BM : TileCfg<1>::BM;
+    const int bn = v == 3 ? TileCfg<3>::BN : (v == 2 || v == 4) ? 64 : TileCfg<1>::BN;
     const long long tiles = (long long)((p.M + bm - 1) / bm) * ((p.N + bn - 1) / bn);
     int S = 1;
     if (variant >= 10) {
@@ -170,13 +183,13 @@ int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, 
     const int b_contig = (layout == kNT) ? p.K : p.N;
     const bool vec = aligned16(p.A) && aligned16(p.B) && (p.lda % 4 == 0) &&
                      (p.ldb % 4 == 0) && (a_contig % 4 == 0) && (b_contig % 4 == 0);
-    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, v == 2 ? 1 : v, vec, s);
+    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
     if (mode != kCordic) return kErrUnsupported;
     if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
     p.k_inv = k_inv_of(p.iters);
     for (int i = 0; i < 24; ++i) p.coef[i] = gemm_coef(i);
     const bool fixed = vec && layout != kTN && (p.iters == 8 || p.iters == 16 || p.iters == 24);
-    if (v == 2 && !fixed) v = 1;       // the 64x64 tile exists for the fixed-n kernels only
+    if ((v == 2 || v == 4) && !fixed) v = 1;   // tiles 2 and 4 exist for the fixed-n kernels only
     if (fixed && p.iters == 8) return pick_fixed<8>(p, layout, v, s);
     if (fixed && p.iters == 16) return pick_fixed<16>(p, layout, v, s);
     if (fixed && p.iters == 24) return pick_fixed<24>(p, layout, v, s);

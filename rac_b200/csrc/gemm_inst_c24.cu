@@ -1,7 +1,8 @@
-// CORDIC GEMM, n = 24 iterations unrolled: NN and NT layouts, vector loads.
+// CORDIC GEMM, n = 24 iterations unrolled: NN and NT layouts, vector loads, tiles 1-4.
 #include "gemm_kernel.cuh"
 namespace racb {
 RACB_GEMM_INST(kCordic, 24, kNN, 1, true) RACB_GEMM_INST(kCordic, 24, kNT, 1, true)
 RACB_GEMM_INST(kCordic, 24, kNN, 3, true) RACB_GEMM_INST(kCordic, 24, kNT, 3, true)
 RACB_GEMM_INST(kCordic, 24, kNN, 2, true) RACB_GEMM_INST(kCordic, 24, kNT, 2, true)
+RACB_GEMM_INST(kCordic, 24, kNN, 4, true) RACB_GEMM_INST(kCordic, 24, kNT, 4, true)
 }

@@ -239,6 +239,8 @@ template <int V> struct TileCfg;
 template <> struct TileCfg<1> { static constexpr int BM = 64, BN = 128, BK = 8, TM = 8, TN = 8, MINB = 4; };
 template <> struct TileCfg<2> { static constexpr int BM = 64, BN = 64, BK = 8, TM = 8, TN = 4, MINB = 6; };
 template <> struct TileCfg<3> { static constexpr int BM = 16, BN = 128, BK = 8, TM = 4, TN = 4, MINB = 4; };
+// 4: 32x64, 4x4 per thread: finer tiles for narrow shards (4096x512 per GPU).
+template <> struct TileCfg<4> { static constexpr int BM = 32, BN = 64, BK = 8, TM = 4, TN = 4, MINB = 8; };
 
 template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
 int launch_inst(const GemmParams& p, cudaStream_t s) {

@@ -179,3 +179,13 @@ def test_splitk_forced_with_epilogue(cuda, orc, layout):
     ref = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=1, **kw).cpu().numpy()
     got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=13, **kw).cpu().numpy()
     assert _normwise(got, ref) <= NORM_TOL
+
+
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("layout", ["nn", "nt"])
+@pytest.mark.parametrize("iters", [8, 16, 24])
+def test_every_tile_variant_bitexact(cuda, orc, variant, layout, iters):
+    M, N, K = 200, 328, 256
+    A, B = _operands(M, N, K, layout, variant * 31 + iters)
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], iters, 1, variant=variant).cpu().numpy()
+    assert np.array_equal(got, orc.gemm(A, B, layout, 1, iters))
