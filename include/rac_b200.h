@@ -34,7 +34,7 @@ extern "C" {
 
 #define RAC_MODE_FAST     0      /* rac_kernels.hip:13 */
 #define RAC_MODE_CORDIC   1      /* rac_kernels.hip:14 */
-#define RAC_MODE_SHIFTADD 2      /* rac_kernels.hip:15 (not provided: RAC_ERR_UNSUPPORTED) */
+#define RAC_MODE_SHIFTADD 2      /* rac_kernels.hip:15 (integer shift-add product) */
 
 #define RAC_ACT_NONE 0           /* rac_torch.cu:665-666 activation ids */
 #define RAC_ACT_RELU 1
@@ -49,7 +49,7 @@ void        rac_clear_error(void);
 /* Process-wide GEMM knobs used by rac_matmul and by launchers given
  * iters <= 0 / mode < 0.  iters is clamped to [1, 24]; iters <= 0 resets to
  * the default.  Defaults: iters = RAC_ITERS (env RAC_CORDIC_ITERS),
- * mode = RAC_MODE_CORDIC (env RAC_CORDIC_MODE = fast|cordic). */
+  * mode = RAC_MODE_CORDIC (env RAC_CORDIC_MODE = fast|cordic|shiftadd). */
 void rac_set_cordic_iters(int iters);
 int  rac_get_cordic_iters(void);
 void rac_set_cordic_mode(int mode);

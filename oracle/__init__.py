@@ -66,6 +66,8 @@ def orc() -> C.CDLL:
         lib.orc_rsqrt.argtypes = [F]
         lib.orc_rsqrt.restype = F
         lib.orc_gemm.argtypes = [_fp, _fp, _fp, I, I, I, I, I, I, L, L]
+        lib.orc_shiftadd_mul.argtypes = [F, F, I]
+        lib.orc_shiftadd_mul.restype = F
         lib.orc_gemm_composed.argtypes = [_fp, _fp, _fp, I, I, I, I, L, L]
         lib.orc_gemm_composed_with.argtypes = [C.c_void_p, _fp, _fp, _fp, I, I, I, I, L, L]
         lib.orc_num_threads.restype = I
@@ -192,7 +194,7 @@ LAYOUTS = {"nn": 0, "nt": 1, "tn": 2}
 
 
 def gemm(A, B, layout: str = "nn", mode: int = 1, iters: int = 16, rows=None):
-    """Sequential-k GEMM of rac_kernels.hip (mode 0 FAST, 1 CORDIC).
+    """Sequential-k GEMM of rac_kernels.hip (mode 0 FAST, 1 CORDIC, 2 SHIFTADD).
 
     Shapes: nn A[M,K] B[K,N]; nt A[M,K] B[N,K]; tn A[K,M] B[K,N].
     rows=(r0, r1) computes only output rows [r0, r1)."""

@@ -256,7 +256,8 @@ void orc_tanh_batch(const float *x, float *y, long n) {
  *
  * layout: 0 = NN (A[M,K], B[K,N]), 1 = NT (B stored [N,K]),
  *         2 = TN (A stored [K,M]).
- * mode:   0 = FAST (sign-XOR FMA, rac_kernels.hip:56-64), 1 = CORDIC.
+ * mode:   0 = FAST (sign-XOR FMA, rac_kernels.hip:56-64), 1 = CORDIC,
+ *         2 = SHIFTADD (rac_kernels.hip:84-122, 217-218).
  */
 static float orc_fma_cordic(float a, float b, float acc, int iters,
                             float k_inv) {
@@ -277,6 +278,38 @@ static float orc_fma_fast(float a, float b, float acc) {
     return fmaf(proj, mag, acc);
 }
 
+/* rac_torch/rac_kernels.hip:84-122 (rac_shiftadd_mul): a*b from the top
+ * `iters` bits of b's 24-bit mantissa by integer shift-and-add, truncated
+ * (no rounding) into an fp32 with sub/super-normal results flushed to 0.
+ * Mode 2 of the GEMM accumulates acc + prod (rac_kernels.hip:217-218). */
+float orc_shiftadd_mul(float a, float b, int iters) {
+    if (a == 0.0f || b == 0.0f) return 0.0f;
+    uint32_t ai, bi; memcpy(&ai, &a, 4); memcpy(&bi, &b, 4);
+    uint32_t sign = (ai ^ bi) & 0x80000000u;
+    int exp_a = (int)((ai >> 23) & 0xFFu) - 127;
+    int exp_b = (int)((bi >> 23) & 0xFFu) - 127;
+    uint32_t ma = 0x00800000u | (ai & 0x007FFFFFu);
+    uint32_t mb = 0x00800000u | (bi & 0x007FFFFFu);
+    uint64_t prod = 0;
+    int lim = iters < 1 ? 1 : (iters > 24 ? 24 : iters);
+    for (int i = 0; i < lim; i++) {
+        uint32_t bit = (mb >> (23 - i)) & 1u;
+        if (bit) prod += ((uint64_t)ma) << (23 - i);
+    }
+    if (prod == 0) return 0.0f;
+    int top = 63 - __builtin_clzll(prod);
+    int shift_r = top - 23;
+    uint32_t mantissa;
+    if (shift_r > 0) mantissa = (uint32_t)(prod >> shift_r) & 0x007FFFFFu;
+    else if (shift_r < 0) mantissa = (uint32_t)(prod << -shift_r) & 0x007FFFFFu;
+    else mantissa = (uint32_t)prod & 0x007FFFFFu;
+    int rexp = exp_a + exp_b + (top - 46) + 127;
+    if (rexp <= 0 || rexp >= 0xFF) return 0.0f;
+    uint32_t bits = sign | ((uint32_t)(rexp & 0xFF) << 23) | mantissa;
+    float r; memcpy(&r, &bits, 4);
+    return r;
+}
+
 void orc_gemm(const float *A, const float *B, float *C, int M, int N, int K,
               int layout, int mode, int iters, long row0, long row1) {
     iters = orc_clamp_iters_gemm(iters);
@@ -289,8 +322,9 @@ void orc_gemm(const float *A, const float *B, float *C, int M, int N, int K,
             for (int k = 0; k < K; k++) {
                 float a = (layout == 2) ? A[(long)k * M + m] : A[m * (long)K + k];
                 float b = (layout == 1) ? B[(long)n * K + k] : B[(long)k * N + n];
-                acc = mode ? orc_fma_cordic(a, b, acc, iters, k_inv)
-                           : orc_fma_fast(a, b, acc);
+                acc = mode == 1 ? orc_fma_cordic(a, b, acc, iters, k_inv)
+                    : mode == 2 ? acc + orc_shiftadd_mul(a, b, iters)
+                    : orc_fma_fast(a, b, acc);
             }
             C[(m - row0) * (long)N + n] = acc;
         }

@@ -10,6 +10,7 @@ namespace racb {
     RACB_GEMM_EXTERN(MODE, ITERS, LAY, 3, false)
 E4(kFast, 0, kNN) E4(kFast, 0, kNT) E4(kFast, 0, kTN)
 E4(kCordic, 0, kNN) E4(kCordic, 0, kNT) E4(kCordic, 0, kTN)
+E4(kShiftAdd, 0, kNN) E4(kShiftAdd, 0, kNT) E4(kShiftAdd, 0, kTN)
 #define E2(ITERS) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 1, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 1, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 3, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 3, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 2, true) \
@@ -184,6 +185,10 @@ int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, 
     const bool vec = aligned16(p.A) && aligned16(p.B) && (p.lda % 4 == 0) &&
                      (p.ldb % 4 == 0) && (a_contig % 4 == 0) && (b_contig % 4 == 0);
     if (mode == kFast) return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
+    if (mode == kShiftAdd) {
+        if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
+        return pick_layout<kShiftAdd, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
+    }
     if (mode != kCordic) return kErrUnsupported;
     if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
     p.k_inv = k_inv_of(p.iters);

@@ -167,6 +167,13 @@ k_gemm(const __grid_constant__ GemmParams p) {
 #pragma unroll
                     for (int j = 0; j < TN; ++j)
                         acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+            } else if constexpr (MODE == kShiftAdd) {
+                // rac_fma_iters SHIFTADD (rac_kernels.hip:217-218): acc + prod.
+#pragma unroll
+                for (int i = 0; i < TM; ++i)
+#pragma unroll
+                    for (int j = 0; j < TN; ++j)
+                        acc[i][j] = __fadd_rn(acc[i][j], shiftadd_mul(a[i], b[j], p.iters));
             } else {
                 uint32_t sgn[TN];
                 float mag[TN];

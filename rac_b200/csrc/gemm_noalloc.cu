@@ -80,7 +80,7 @@ RAC_API int rac_gemm_splitk_noalloc_async(const float* A, long long lda, const f
     if (M <= 0 || N <= 0 || K <= 0 || splits < 0)
         return record_status(kErrInvalidDim, "rac_gemm_splitk_noalloc_async: invalid dimension");
     if (layout < kNN || layout > kTN || act < kActNone || act > kActSilu ||
-        (mode != kFast && mode != kCordic))
+        (mode != kFast && mode != kCordic && mode != kShiftAdd))
         return record_status(kErrUnsupported, "rac_gemm_splitk_noalloc_async: unsupported layout/mode/act");
     if (beta != 0.0f && !Cin) Cin = C;
 

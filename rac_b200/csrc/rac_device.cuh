@@ -216,6 +216,37 @@ __device__ __forceinline__ bool cordic_rotate_rt(float& xr, float& yr, float the
     return ok;
 }
 
+// rac_shiftadd_mul (rac_torch/rac_kernels.hip:84-122): a * b from the top
+// `iters` bits of b's 24-bit mantissa by integer shift-and-add on the
+// INT pipe (no FP multiplier), truncated into fp32, sub/super-normal results
+// flushed to 0.  The 48-bit product is kept as two 32-bit words.
+__device__ __forceinline__ float shiftadd_mul(float a, float b, int iters) {
+    if (a == 0.0f || b == 0.0f) return 0.0f;
+    const uint32_t ai = __float_as_uint(a), bi = __float_as_uint(b);
+    const uint32_t sign = (ai ^ bi) & 0x80000000u;
+    const int exp_a = (int)((ai >> 23) & 0xFFu) - 127;
+    const int exp_b = (int)((bi >> 23) & 0xFFu) - 127;
+    const uint32_t ma = 0x00800000u | (ai & 0x007FFFFFu);
+    const uint32_t mb = 0x00800000u | (bi & 0x007FFFFFu);
+    const int lim = iters < 1 ? 1 : (iters > 24 ? 24 : iters);
+    unsigned long long prod = 0ull;
+    for (int i = 0; i < lim; ++i) {
+        const int sh = 23 - i;
+        const unsigned long long term = ((unsigned long long)ma) << sh;
+        prod += ((mb >> sh) & 1u) ? term : 0ull;
+    }
+    if (prod == 0ull) return 0.0f;
+    const int top = 63 - __clzll((long long)prod);
+    const int shift_r = top - 23;
+    uint32_t mantissa;
+    if (shift_r > 0) mantissa = (uint32_t)(prod >> shift_r) & 0x007FFFFFu;
+    else if (shift_r < 0) mantissa = (uint32_t)(prod << -shift_r) & 0x007FFFFFu;
+    else mantissa = (uint32_t)prod & 0x007FFFFFu;
+    const int rexp = exp_a + exp_b + (top - 46) + 127;
+    if (rexp <= 0 || rexp >= 0xFF) return 0.0f;
+    return __uint_as_float(sign | ((uint32_t)(rexp & 0xFF) << 23) | mantissa);
+}
+
 // 1/K(n) in float, as both reference libraries compute it at run time
 // (lib/c/rac_cpu.c:277, rac_kernels.hip:182).
 __host__ __device__ inline float k_inv_of(int iters) {

@@ -60,6 +60,7 @@ void init_knobs() {
         int m = kCordic;
         if (const char* e = std::getenv("RAC_CORDIC_MODE")) {
             if (!std::strcmp(e, "fast") || !std::strcmp(e, "0")) m = kFast;
+            if (!std::strcmp(e, "shiftadd") || !std::strcmp(e, "2")) m = kShiftAdd;
         }
         int expected = -1;
         g_mode.compare_exchange_strong(expected, m);
@@ -171,7 +172,7 @@ RAC_API int rac_get_cordic_iters(void) { init_knobs(); return g_iters.load(); }
 RAC_API void rac_set_cordic_mode(int mode) {
     // rac_torch_bind.cpp:216-219: out-of-range modes fall back to FAST.
     init_knobs();
-    g_mode.store(mode == kCordic ? kCordic : kFast);
+    g_mode.store((mode == kCordic || mode == kShiftAdd) ? mode : kFast);
 }
 RAC_API int rac_get_cordic_mode(void) { init_knobs(); return g_mode.load(); }
 

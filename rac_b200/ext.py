@@ -44,7 +44,7 @@ def get_cordic_iters() -> int:
 def set_cordic_mode(mode: int) -> None:
     """rac_torch_bind.cpp:216-219: unknown modes fall back to FAST."""
     global _mode
-    _mode = mode if mode in (MODE_FAST, MODE_CORDIC) else MODE_FAST
+    _mode = mode if mode in (MODE_FAST, MODE_CORDIC, MODE_SHIFTADD) else MODE_FAST
 
 
 def get_cordic_mode() -> int:
@@ -54,8 +54,6 @@ def get_cordic_mode() -> int:
 def _resolve(iters: int, mode: int) -> tuple[int, int]:
     it = _iters if iters <= 0 else max(1, min(24, int(iters)))
     md = _mode if mode < 0 else int(mode)
-    if md == MODE_SHIFTADD:
-        raise _lib.RacError(-5, "SHIFTADD mode is not provided by librac_b200")
     return it, md
 
 

@@ -65,8 +65,8 @@ _RAC_CORDIC_MODE = _resolve_mode(os.environ.get("RAC_CORDIC_MODE", "fast"))
 
 
 def rac_set_mode(mode) -> None:
-    """'fast' (sign-XOR FMA) or 'cordic' (iterative micro-rotations).
-    'shiftadd' is accepted but raises at the first matmul (not provided)."""
+    """'fast' (sign-XOR FMA), 'cordic' (iterative micro-rotations) or
+    'shiftadd' (integer shift-add product, rac_kernels.hip:84-122)."""
     global _RAC_CORDIC_MODE
     _RAC_CORDIC_MODE = _resolve_mode(mode)
     ext.set_cordic_mode(_RAC_CORDIC_MODE)

@@ -52,6 +52,8 @@ def test_knobs():
     assert L.rac_get_cordic_mode() == 0
     L.rac_set_cordic_mode(7)
     assert L.rac_get_cordic_mode() == 0
+    L.rac_set_cordic_mode(2)
+    assert L.rac_get_cordic_mode() == 2
     L.rac_set_cordic_mode(1)
     assert L.rac_get_cordic_mode() == 1
 

@@ -189,3 +189,24 @@ def test_every_tile_variant_bitexact(cuda, orc, variant, layout, iters):
     A, B = _operands(M, N, K, layout, variant * 31 + iters)
     got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], iters, 1, variant=variant).cpu().numpy()
     assert np.array_equal(got, orc.gemm(A, B, layout, 1, iters))
+
+
+@pytest.mark.parametrize("layout", ["nn", "nt", "tn"])
+@pytest.mark.parametrize("iters", [4, 8, 16, 24])
+@pytest.mark.parametrize("shape", [(63, 65, 67), (128, 96, 160), (16, 200, 96)])
+def test_shiftadd_bitexact(cuda, orc, layout, iters, shape):
+    """SHIFTADD (rac_kernels.hip:84-122, 217-218): integer shift-add products,
+    bit-exact to the CPU restatement."""
+    M, N, K = shape
+    A, B = _operands(M, N, K, layout, iters + M)
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], iters, 2).cpu().numpy()
+    assert np.array_equal(got, orc.gemm(A, B, layout, 2, iters))
+
+
+def test_shiftadd_edge_values(cuda, orc):
+    """Zeros, tiny products flushed to 0, huge products flushed to 0."""
+    A = np.array([[0.0, 1e-30, 3e30, -2.5, 1.0]], np.float32)
+    B = np.array([[1.0], [1e-20], [4e20], [-0.0], [0.1]], np.float32)
+    for it in (1, 8, 24):
+        got = ext.gemm(_t(A, cuda), _t(B, cuda), LAYOUT_NN, it, 2).cpu().numpy()
+        assert np.array_equal(got, orc.gemm(A, B, "nn", 2, it))

@@ -152,3 +152,30 @@ def test_cpu_tensors_are_rejected():
     lin = R.RACLinear(4, 4)
     with pytest.raises(ValueError):
         lin(torch.randn(2, 4))
+
+
+@pytest.mark.parametrize("mode,gated", [("fast", False), ("cordic", False), ("cordic", True)])
+def test_llama_block_training_decreases_loss(cuda, mode, gated):
+    """rac_torch/test_rac_dvt.py:897-923 (DVT-31): 20 Adam steps lower the loss by
+    >= 5 %; every projection's forward and backward GEMM runs on the RAC kernels
+    (NT forward, NN grad-input, TN grad-weight)."""
+    R.rac_set_mode(mode)
+    R.rac_set_precision(16)
+    try:
+        torch.manual_seed(0)
+        block = R.RACLlamaBlock(d_model=32, n_heads=4, ff_dim=64, max_seq_len=16, gated=gated).to(cuda)
+        opt = torch.optim.Adam(block.parameters(), lr=1e-3)
+        x = torch.randn(2, 8, 32, device=cuda)
+        target = torch.randn_like(x)
+        losses = []
+        for _ in range(20):
+            opt.zero_grad()
+            loss = (block(x, is_causal=True) - target).pow(2).mean()
+            loss.backward()
+            opt.step()
+            losses.append(loss.item())
+        assert losses[-1] < losses[0] * 0.95, losses
+        with torch.no_grad():
+            assert torch.isfinite(block(x)).all()
+    finally:
+        R.rac_set_mode("fast")

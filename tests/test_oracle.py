@@ -149,3 +149,16 @@ def test_restatement_vs_reference_library_random(orc):
     assert np.array_equal(orc.rotate_batch(v, th, 16, True), orc.ref_rotate_batch(v, th))
     x = (rng.standard_normal((64, 777)) * 3).astype(np.float32)
     assert np.array_equal(orc.softmax(x), orc.ref_softmax(x))
+
+
+def test_shiftadd_restatement_properties(orc):
+    """rac_shiftadd_mul at 24 bits is the exact product truncated to 24 bits;
+    fewer bits never increase |a*b| (rac_kernels.hip:66-83 error model)."""
+    L = orc.orc()
+    rng = np.random.default_rng(11)
+    for a, b in rng.uniform(-4, 4, (500, 2)).astype(np.float32):
+        p24 = L.orc_shiftadd_mul(float(a), float(b), 24)
+        exact = float(a) * float(b)
+        assert abs(p24 - exact) <= abs(exact) * 2 ** -23
+        p8 = L.orc_shiftadd_mul(float(a), float(b), 8)
+        assert abs(p8) <= abs(p24) and abs(p8 - exact) <= abs(exact) * 2 ** -7
