@@ -82,7 +82,7 @@ void   rac_rotate_batch(float2 *v, float *theta, float2 *out, int n);
  * RAC_ITERS). */
 void   rac_matmul(float *A, float *B, float *C, int M, int N, int K);
 
-/* ── 7. transformer primitives (ref rac.h:274-320) ──────────────────────── */
+/* ── 7. transformer primitives (ref rac.h:274-335) ──────────────────────── */
 float  rac_rsqrt(float x);
 float  rac_sigmoid(float x);
 void   rac_sincos(float theta, float *s, float *c);
@@ -94,6 +94,11 @@ void   rac_rope_cache(float *cos_out, float *sin_out, int max_seq,
                       int head_dim, float base);
 void   rac_rope_apply(float *x, const float *cos_tab, const float *sin_tab,
                       int batch, int n_heads, int seq, int head_dim);
+/* ref rac.h:330-335.  q, k, v, out [batch, n_heads, seq, head_dim];
+ * head_dim in {32, 64, 128}; mask optional [seq, seq] additive. */
+void   rac_attention(const float *q, const float *k, const float *v,
+                     const float *mask, int is_causal, float *out,
+                     int batch, int n_heads, int seq, int head_dim);
 
 /* ── 8. tunable precision (ref rac.h:345-346) ───────────────────────────── */
 float2 rac_rotate_precision(float2 v, float theta, int iters);

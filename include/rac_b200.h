@@ -148,6 +148,11 @@ int rac_rope_cache_async(float *cos_out, float *sin_out, int max_seq, int head_d
 int rac_rope_apply_async(float *x, const float *cos_tab, const float *sin_tab,
                          const int *pos, long long batch_heads, int seq, int head_dim,
                          int form, void *stream);
+/* Fused attention on `stream` (device pointers): rac_attention without the
+ * [seq, seq] score tensor (lib/c/rac_cpu.c:637-703 semantics). */
+int rac_attention_async(const float *q, const float *k, const float *v, const float *mask,
+                        int is_causal, float *out, int batch, int n_heads, int seq,
+                        int head_dim, void *stream);
 /* Reads and clears the device's error word (bounded-loop overruns) after
  * synchronising `stream`; returns RAC_OK or RAC_ERR_DEVICE. */
 int rac_check_device_errors(void *stream);
@@ -160,6 +165,8 @@ typedef struct { const float *x; float *y; const float *gamma, *beta; float eps;
 typedef struct { float *x; const float *cos_tab, *sin_tab; int batch, n_heads, seq, head_dim; } rac_rope_apply_desc;
 typedef struct { float *cos_out, *sin_out; int max_seq, head_dim; float base; } rac_rope_cache_desc;
 typedef struct { const float *x; float *y; int n; } rac_unary_desc;
+typedef struct { const float *q, *k, *v, *mask; int is_causal; float *out;
+                 int batch, n_heads, seq, head_dim; } rac_attention_desc;
 
 #ifdef __cplusplus
 }

@@ -66,6 +66,7 @@ def orc() -> C.CDLL:
         lib.orc_rsqrt.argtypes = [F]
         lib.orc_rsqrt.restype = F
         lib.orc_gemm.argtypes = [_fp, _fp, _fp, I, I, I, I, I, I, L, L]
+        lib.orc_attention.argtypes = [_fp, _fp, _fp, _fp, I, _fp, I, I, I, I]
         lib.orc_shiftadd_mul.argtypes = [F, F, I]
         lib.orc_shiftadd_mul.restype = F
         lib.orc_gemm_composed.argtypes = [_fp, _fp, _fp, I, I, I, I, L, L]
@@ -209,6 +210,30 @@ def gemm(A, B, layout: str = "nn", mode: int = 1, iters: int = 16, rows=None):
     C_ = np.empty((r1 - r0, N), np.float32)
     orc().orc_gemm(_p(A), _p(B), _p(C_), M, N, K, lay, mode, iters, r0, r1)
     return C_
+
+
+def attention(q, k, v, mask=None, is_causal=False):
+    """rac_scaled_dot_attention restated; q, k, v: [b, h, s, hd]."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.empty_like(q)
+    m = _p(_f32(mask)) if mask is not None else None
+    b, h, s, hd = q.shape
+    orc().orc_attention(_p(q), _p(k), _p(v), m, int(is_causal), _p(out), b, h, s, hd)
+    return out
+
+
+def ref_attention(q, k, v, mask=None, is_causal=False):
+    """The reference library's own rac_scaled_dot_attention."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.empty_like(q)
+    L = ref()
+    L.rac_scaled_dot_attention.argtypes = [_fp, _fp, _fp, _fp, C.c_int, _fp, C.c_int, C.c_int,
+                                           C.c_int, C.c_int, C.c_void_p]
+    L.rac_scaled_dot_attention.restype = C.c_int
+    b, h, s, hd = q.shape
+    m = _p(_f32(mask)) if mask is not None else None
+    assert L.rac_scaled_dot_attention(_p(q), _p(k), _p(v), m, int(is_causal), _p(out), b, h, s, hd, None) == 0
+    return out
 
 
 def gemm_composed(A, B, iters: int = 16, rows=None):

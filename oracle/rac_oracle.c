@@ -246,6 +246,47 @@ void orc_tanh_batch(const float *x, float *y, long n) {
     for (long i = 0; i < n; i++) y[i] = tanhf(x[i]);
 }
 
+/* lib/c/rac_cpu.c:637-703 (rac_scaled_dot_attention): scores = (q.k)*scale
+ * with fmaf over d, causal -inf above the diagonal, optional additive
+ * [seq, seq] mask, row softmax (max, expf, sum, inv = sum > 0 ? 1/sum : 0),
+ * out = sum_s fmaf(p, v, acc).  q, k, v, out: [batch, heads, seq, hd]. */
+void orc_attention(const float *q, const float *k, const float *v, const float *mask,
+                   int is_causal, float *out, int batch, int heads, int seq, int hd) {
+    float scale = 1.0f / sqrtf((float)hd);
+    #pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int b = 0; b < batch; b++) {
+        for (int h = 0; h < heads; h++) {
+            float *row = (float *)malloc((size_t)seq * sizeof(float));
+            long base = ((long)(b * heads + h) * seq) * hd;
+            const float *qb = q + base, *kb = k + base, *vb = v + base;
+            float *ob = out + base;
+            for (int t = 0; t < seq; t++) {
+                for (int s2 = 0; s2 < seq; s2++) {
+                    float acc = 0.0f;
+                    for (int d = 0; d < hd; d++)
+                        acc = fmaf(qb[(long)t * hd + d], kb[(long)s2 * hd + d], acc);
+                    float sc = acc * scale;
+                    if (is_causal && s2 > t) sc = -INFINITY;
+                    if (mask) sc += mask[(long)t * seq + s2];
+                    row[s2] = sc;
+                }
+                float m = row[0];
+                for (int s2 = 1; s2 < seq; s2++) if (row[s2] > m) m = row[s2];
+                float sum = 0.0f;
+                for (int s2 = 0; s2 < seq; s2++) { row[s2] = expf(row[s2] - m); sum += row[s2]; }
+                float inv = (sum > 0.0f) ? 1.0f / sum : 0.0f;
+                for (int s2 = 0; s2 < seq; s2++) row[s2] *= inv;
+                for (int d = 0; d < hd; d++) {
+                    float acc = 0.0f;
+                    for (int s2 = 0; s2 < seq; s2++) acc = fmaf(row[s2], vb[(long)s2 * hd + d], acc);
+                    ob[(long)t * hd + d] = acc;
+                }
+            }
+            free(row);
+        }
+    }
+}
+
 /* ── GEMM ──────────────────────────────────────────────────────────────────
  * rac_torch/rac_kernels.hip:139-185 (rac_cordic_rotate_n + rac_fma_cordic):
  * one MAC rotates (a, 0) by angle(b) in {0, pi}, runs `iters` micro-rotations,

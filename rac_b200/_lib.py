@@ -99,6 +99,8 @@ _SIGS = {
     "rac_rope_cache_async": (_i, [_vp, _vp, _i, _i, _f, _vp]),
     "rac_rope_apply_async": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _i, _i, _vp]),
     "rac_check_device_errors": (_i, [_vp]),
+    "rac_attention": (None, [_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i]),
+    "rac_attention_async": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _vp]),
 }
 
 

@@ -1,0 +1,233 @@
+// attention.cu -- fused scaled-dot-product attention (rac_attention), sm_100a.
+//
+// Semantics: lib/c/rac_cpu.c:637-703 (rac_scaled_dot_attention):
+//   score[t,s] = fmaf-accumulated q_t . k_s (d ascending) * (1/sqrtf(hd)),
+//   -inf where causal and s > t, + mask[t,s] when a mask is given,
+//   p = expf(score - rowmax) / sum,  out_t = sum_s p[t,s] * v_s (s ascending).
+//
+// One CTA owns 64 query rows of one (batch, head) and streams the keys in
+// 64-row tiles through shared memory; the [seq, seq] score matrix never
+// exists in HBM.  Pass 1 recomputes the scores only for the exact row max
+// (max is order independent); pass 2 recomputes them, forms e = expf(s - max),
+// the row sum, and accumulates O += e * V key by key in ascending order, then
+// scales by 1/sum.  So the scores are bit-identical to the reference and the
+// output differs from it only by expf's last bit and the sum's association
+// (the reference multiplies by 1/sum before accumulating).  Recomputing the
+// scores (instead of online rescaling) keeps the output deterministic and
+// that close to the reference for 1.5x the FLOPs of a single pass.
+//
+// 128 threads: for the 64x64 score tile a thread owns rows 4*rg..4*rg+3 and
+// columns cg + 8j (j < 8); for the 64 x HD output it owns the same rows and
+// HD/8 columns in float4 groups.  Shared rows are padded by 4 floats so that
+// the float4 reads of K, V and P are bank-conflict free.
+#include <cmath>
+
+#include "rac_internal.h"
+#include "stream_ops.h"
+
+namespace racb {
+
+constexpr int kAttBQ = 64, kAttBK = 64, kAttThreads = 128;
+
+template <int HD>
+struct AttSmem {
+    static constexpr int LD = HD + 4;             // padded row (floats)
+    static constexpr int PLD = kAttBK + 4;
+    static constexpr size_t bytes = sizeof(float) * (2 * kAttBQ * LD + kAttBQ * PLD);
+};
+
+template <int HD>
+__device__ __forceinline__ void load_tile(float* dst, const float* __restrict__ src, int row0,
+                                          int rows_valid) {
+    constexpr int LD = AttSmem<HD>::LD;
+    constexpr int QPR = HD / 4;                   // float4 per row
+    for (int e = threadIdx.x; e < kAttBQ * QPR; e += kAttThreads) {
+        const int r = e / QPR, c = (e % QPR) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row0 + r < rows_valid) v = __ldg(reinterpret_cast<const float4*>(src + (long long)(row0 + r) * HD + c));
+        *reinterpret_cast<float4*>(dst + r * LD + c) = v;
+    }
+}
+
+// Scores of this thread's 4 x 8 block for the key tile in Ks, after scale,
+// causal and mask (keys beyond seq -> -inf).
+template <int HD>
+__device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, const float* Ks,
+                                            int t0, int s0, int seq, float scale, int causal,
+                                            const float* __restrict__ mask) {
+    constexpr int LD = AttSmem<HD>::LD;
+    const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc[i][j] = 0.0f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+        float4 q[4], k[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg * 4 + i) * LD + d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * LD + d);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float a = sc[i][j];
+                a = __fmaf_rn(q[i].x, k[j].x, a);
+                a = __fmaf_rn(q[i].y, k[j].y, a);
+                a = __fmaf_rn(q[i].z, k[j].z, a);
+                a = __fmaf_rn(q[i].w, k[j].w, a);
+                sc[i][j] = a;
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + rg * 4 + i;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int s = s0 + cg + 8 * j;
+            float v = __fmul_rn(sc[i][j], scale);
+            if (causal && s > t) v = -INFINITY;
+            if (mask && t < seq && s < seq) v = __fadd_rn(v, mask[(long long)t * seq + s]);
+            if (s >= seq) v = -INFINITY;
+            sc[i][j] = v;
+        }
+    }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttThreads, 2)
+k_attention(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+            const float* __restrict__ mask, int causal, float* __restrict__ out, int heads, int seq,
+            float scale) {
+    constexpr int LD = AttSmem<HD>::LD, PLD = AttSmem<HD>::PLD, CG = HD / 32;
+    extern __shared__ __align__(16) float smem[];
+    float* Qs = smem;
+    float* KVs = Qs + kAttBQ * LD;
+    float* Ps = KVs + kAttBQ * LD;
+
+    const int nqb = (seq + kAttBQ - 1) / kAttBQ;
+    const int qb = nqb - 1 - blockIdx.x;          // heaviest (causal) blocks first
+    const long long bh = (long long)blockIdx.z * heads + blockIdx.y;
+    const float* qh = q + bh * seq * HD;
+    const float* kh = k + bh * seq * HD;
+    const float* vh = v + bh * seq * HD;
+    float* oh = out + bh * seq * HD;
+    const int t0 = qb * kAttBQ;
+    const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
+    const int nkb = causal ? min(qb + 1, (seq + kAttBK - 1) / kAttBK) : (seq + kAttBK - 1) / kAttBK;
+
+    load_tile<HD>(Qs, qh, t0, seq);
+
+    // Pass 1: exact row max.
+    float mrow[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    for (int kb = 0; kb < nkb; ++kb) {
+        __syncthreads();
+        load_tile<HD>(KVs, kh, kb * kAttBK, seq);
+        __syncthreads();
+        float sc[4][8];
+        tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mrow[i] = fmaxf(mrow[i], sc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) mrow[i] = fmaxf(mrow[i], __shfl_xor_sync(0xffffffffu, mrow[i], o));
+
+    // Pass 2: e = expf(s - max), row sums, O += e V in key order.
+    float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+    float4 o[4][CG];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int g = 0; g < CG; ++g) o[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int kb = 0; kb < nkb; ++kb) {
+        __syncthreads();
+        load_tile<HD>(KVs, kh, kb * kAttBK, seq);
+        __syncthreads();
+        float sc[4][8];
+        tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float e = expf(__fsub_rn(sc[i][j], mrow[i]));
+                lsum[i] = __fadd_rn(lsum[i], e);
+                Ps[(rg * 4 + i) * PLD + cg + 8 * j] = e;
+            }
+        __syncthreads();
+        load_tile<HD>(KVs, vh, kb * kAttBK, seq);
+        __syncthreads();
+        const int kmax = min(kAttBK, seq - kb * kAttBK);
+        for (int s = 0; s < kmax; ++s) {
+            float p[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = Ps[(rg * 4 + i) * PLD + s];
+#pragma unroll
+            for (int g = 0; g < CG; ++g) {
+                const float4 vv = *reinterpret_cast<const float4*>(KVs + s * LD + cg * 4 + 32 * g);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    o[i][g].x = __fmaf_rn(p[i], vv.x, o[i][g].x);
+                    o[i][g].y = __fmaf_rn(p[i], vv.y, o[i][g].y);
+                    o[i][g].z = __fmaf_rn(p[i], vv.z, o[i][g].z);
+                    o[i][g].w = __fmaf_rn(p[i], vv.w, o[i][g].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) lsum[i] = __fadd_rn(lsum[i], __shfl_xor_sync(0xffffffffu, lsum[i], off));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + rg * 4 + i;
+        if (t >= seq) continue;
+        const float inv = lsum[i] > 0.0f ? __fdiv_rn(1.0f, lsum[i]) : 0.0f;
+#pragma unroll
+        for (int g = 0; g < CG; ++g) {
+            const float4 r = o[i][g];
+            *reinterpret_cast<float4*>(oh + (long long)t * HD + cg * 4 + 32 * g) =
+                make_float4(__fmul_rn(r.x, inv), __fmul_rn(r.y, inv), __fmul_rn(r.z, inv), __fmul_rn(r.w, inv));
+        }
+    }
+}
+
+template <int HD>
+static int launch_att(const float* q, const float* k, const float* v, const float* mask, int causal,
+                      float* out, int batch, int heads, int seq, float scale, cudaStream_t s) {
+    const size_t smem = AttSmem<HD>::bytes;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return kErrCuda;
+        attr_set[dev] = true;
+    }
+    const dim3 grid((seq + kAttBQ - 1) / kAttBQ, heads, batch);
+    if (grid.y > 65535 || grid.z > 65535) return kErrInvalidDim;
+    k_attention<HD><<<grid, kAttThreads, smem, s>>>(q, k, v, mask, causal, out, heads, seq, scale);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int attention(const float* q, const float* k, const float* v, const float* mask, int causal,
+              float* out, int batch, int heads, int seq, int head_dim, cudaStream_t s) {
+    if (!q || !k || !v || !out) return kErrNullPtr;
+    if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0) return kErrInvalidDim;
+    for (const void* p : {(const void*)q, (const void*)k, (const void*)v, (const void*)out})
+        if (reinterpret_cast<uintptr_t>(p) & 15u) return kErrUnsupported;
+    const float scale = 1.0f / sqrtf((float)head_dim);   // rac_cpu.c:646
+    switch (head_dim) {
+        case 32: return launch_att<32>(q, k, v, mask, causal, out, batch, heads, seq, scale, s);
+        case 64: return launch_att<64>(q, k, v, mask, causal, out, batch, heads, seq, scale, s);
+        case 128: return launch_att<128>(q, k, v, mask, causal, out, batch, heads, seq, scale, s);
+        default: return kErrUnsupported;
+    }
+}
+
+}  // namespace racb

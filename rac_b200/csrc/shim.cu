@@ -500,6 +500,33 @@ RAC_API void rac_rope_apply(float* x, const float* cos_tab, const float* sin_tab
     set_status(do_rope_apply(x, cos_tab, sin_tab, batch, n_heads, seq, head_dim), "rac_rope_apply");
 }
 
+RAC_API int rac_attention_async(const float* q, const float* k, const float* v, const float* mask,
+                                int is_causal, float* out, int batch, int n_heads, int seq,
+                                int head_dim, void* stream) {
+    return set_status(attention(q, k, v, mask, is_causal, out, batch, n_heads, seq, head_dim,
+                                as_stream(stream)), "rac_attention_async");
+}
+
+static int do_attention(const float* q, const float* k, const float* v, const float* mask,
+                        int causal, float* out, int batch, int heads, int seq, int hd) {
+    if (!q || !k || !v || !out) return kErrNullPtr;
+    if (batch <= 0 || heads <= 0 || seq <= 0 || hd <= 0) return kErrInvalidDim;
+    Call c;
+    if (c.begin() != kOk) return c.st;
+    const size_t bytes = sizeof(float) * (size_t)batch * heads * seq * hd;
+    auto dq = (const float*)c.map(q, bytes, true, false);
+    auto dk = (const float*)c.map(k, bytes, true, false);
+    auto dv = (const float*)c.map(v, bytes, true, false);
+    auto dm = (const float*)c.map(mask, sizeof(float) * (size_t)seq * seq, true, false);
+    auto dout = (float*)c.map(out, bytes, false, true);
+    int st = c.st == kOk ? attention(dq, dk, dv, dm, causal, dout, batch, heads, seq, hd, c.s) : c.st;
+    return c.finish(st, false);
+}
+RAC_API void rac_attention(const float* q, const float* k, const float* v, const float* mask,
+                           int is_causal, float* out, int batch, int n_heads, int seq, int head_dim) {
+    set_status(do_attention(q, k, v, mask, is_causal, out, batch, n_heads, seq, head_dim), "rac_attention");
+}
+
 // ── context API (rac.h:85-88) ───────────────────────────────────────────
 
 struct rac_context_t { rac_backend backend; int device; };
@@ -523,7 +550,7 @@ RAC_API int rac_query_capability(rac_context ctx, rac_op_type op) {
         case RAC_OP_ROTATE: case RAC_OP_EXP: case RAC_OP_TANH: case RAC_OP_SOFTMAX:
         case RAC_OP_ROTATE_BATCH: case RAC_OP_MATMUL: case RAC_OP_RSQRT: case RAC_OP_SIGMOID:
         case RAC_OP_SINCOS: case RAC_OP_LAYERNORM: case RAC_OP_RMSNORM: case RAC_OP_ROPE_CACHE:
-        case RAC_OP_ROPE_APPLY:
+        case RAC_OP_ROPE_APPLY: case RAC_OP_ATTENTION:
             return 1;
         default:
             return 0;
@@ -577,6 +604,12 @@ RAC_API int rac_execute(rac_context ctx, rac_op_type op, void* desc) {
             const int u = op == RAC_OP_EXP ? kUnaryExp : op == RAC_OP_TANH ? kUnaryTanh
                         : op == RAC_OP_RSQRT ? kUnaryRsqrt : kUnarySigmoid;
             set_status(do_unary(d->x, d->y, d->n, u), "rac_execute");
+            break;
+        }
+        case RAC_OP_ATTENTION: {
+            auto* d = static_cast<rac_attention_desc*>(desc);
+            rac_attention(d->q, d->k, d->v, d->mask, d->is_causal, d->out, d->batch, d->n_heads,
+                          d->seq, d->head_dim);
             break;
         }
         default:

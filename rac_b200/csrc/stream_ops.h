@@ -26,4 +26,9 @@ int rmsnorm_rows(const float* x, float* y, const float* gamma, float eps, long l
 int layernorm_rows(const float* x, float* y, const float* gamma, const float* beta, float eps,
                    long long rows, int d, cudaStream_t s);
 
+// Fused attention (attention.cu), q/k/v/out [batch, heads, seq, head_dim]
+// contiguous; mask optional [seq, seq]; head_dim in {32, 64, 128}.
+int attention(const float* q, const float* k, const float* v, const float* mask, int causal,
+              float* out, int batch, int heads, int seq, int head_dim, cudaStream_t s);
+
 }  // namespace racb

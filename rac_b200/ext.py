@@ -338,6 +338,21 @@ def rope_apply_(x: torch.Tensor, cos_tab: torch.Tensor, sin_tab: torch.Tensor,
     return x
 
 
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor | None = None,
+              is_causal: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused softmax(q k^T / sqrt(hd) + mask) v on [B, H, S, hd] (rac_attention)."""
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    m = _prep(mask) if mask is not None else None
+    if m is not None and m.shape != (q.shape[-2], q.shape[-2]):
+        raise ValueError("attention mask must be [seq, seq]")
+    o = torch.empty_like(q) if out is None else out
+    b, h, s_, hd = q.shape
+    with torch.cuda.device(q.device):
+        _lib.call("rac_attention_async", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(m),
+                  int(bool(is_causal)), o.data_ptr(), b, h, s_, hd, _stream(q))
+    return o
+
+
 def check_device_errors(device=None) -> None:
     """Synchronises the current stream and raises if a bounded device loop gave up."""
     dev = torch.device("cuda") if device is None else torch.device(device)

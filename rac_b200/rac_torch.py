@@ -375,9 +375,10 @@ class RACLayerNorm(nn.Module):
 
 class RACRoPEAttention(nn.Module):
     """Llama-style attention (rac_torch.py:1279-1343): fused qkv RACLinear, RoPE on
-    Q and K, softmax(QK^T * scale + mask) V, out_proj RACLinear.  As in the
-    reference module, the two attention products use torch.matmul in fp32;
-    the softmax runs on this library's row kernel."""
+    Q and K, softmax(QK^T * scale + mask) V, out_proj RACLinear.  In inference
+    the attention core is this library's fused kernel (rac_attention, no
+    [B, H, T, T] tensor); under autograd it is torch.matmul + softmax in fp32,
+    as in the reference module."""
 
     def __init__(self, d_model: int, n_heads: int, max_seq_len: int = 4096, bias: bool = False,
                  dropout: float = 0.0, rope_base: float = 10000.0, device=None, dtype=None):
@@ -402,6 +403,14 @@ class RACRoPEAttention(nn.Module):
         k = k.view(B, T, H, self.d_head).transpose(1, 2)
         v = v.view(B, T, H, self.d_head).transpose(1, 2)
         q, k = self.rope(q, k, positions=positions)
+        fused_ok = (not torch.is_grad_enabled() and isinstance(self.dropout, nn.Identity)
+                    and self.d_head in (32, 64, 128)
+                    and (mask is None or tuple(mask.shape) == (T, T)))
+        if fused_ok:
+            # One streaming kernel: no [B, H, T, T] score tensor (rac_attention).
+            m = mask.to(device=x.device, dtype=torch.float32).contiguous() if mask is not None else None
+            out = ext.attention(q, k, v.contiguous(), m, is_causal)
+            return out.transpose(1, 2).reshape(B, T, H * self.d_head)
         scores = torch.matmul(q, k.transpose(-2, -1)) * self.scale
         if is_causal:
             scores = scores + torch.triu(torch.full((T, T), float("-inf"), device=x.device,

@@ -65,6 +65,11 @@ def lib_vectors(out: str) -> None:
     for it in (8, 16, 24):
         d[f"mm_cordic{it}"] = O.gemm_composed_ref(A, B, it)
     d["mm_sgemm"] = O.ref_sgemm(A, B)
+    qa, ka, va = [rng.standard_normal((1, 2, 70, 64)).astype(np.float32) for _ in range(3)]
+    am = (rng.standard_normal((70, 70)) * 0.5).astype(np.float32)
+    d["att_q"], d["att_k"], d["att_v"], d["att_mask"] = qa, ka, va, am
+    d["att_causal"] = O.ref_attention(qa, ka, va, None, True)
+    d["att_masked"] = O.ref_attention(qa, ka, va, am, False)
     np.savez_compressed(out, **d)
 
 

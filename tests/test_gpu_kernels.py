@@ -222,3 +222,27 @@ def test_rotate_direction_edge_angles(cuda, orc, it):
     assert _bits_equal(got, orc.rotate_batch(v, th, it, False))
     got = ext.project_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
     assert _bits_equal(got, orc.project_batch(v, th, it))
+
+
+# ── fused attention ─────────────────────────────────────────────────────
+
+def test_attention_golden_host_abi(cuda, golden):
+    """rac_attention (rac.h:330-335) with host buffers vs the reference library."""
+    L = _lib.lib()
+    q, k, v, m = golden["att_q"], golden["att_k"], golden["att_v"], golden["att_mask"]
+    out = np.zeros_like(q)
+    L.rac_attention(_p(q), _p(k), _p(v), None, 1, _p(out), *q.shape)
+    _lib.check()
+    assert O.max_rel_err(out, golden["att_causal"]) <= 1e-4
+    L.rac_attention(_p(q), _p(k), _p(v), _p(m), 0, _p(out), *q.shape)
+    _lib.check()
+    assert O.max_rel_err(out, golden["att_masked"]) <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 64, 128), (1, 4, 200, 64), (2, 2, 1, 32), (1, 1, 129, 128)])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_attention_vs_oracle(cuda, orc, shape, causal):
+    rng = np.random.default_rng(sum(shape) + causal)
+    q, k, v = [rng.standard_normal(shape).astype(np.float32) for _ in range(3)]
+    got = ext.attention(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, bool(causal)).cpu().numpy()
+    assert O.max_rel_err(got, orc.attention(q, k, v, None, causal)) <= 1e-4

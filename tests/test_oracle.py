@@ -162,3 +162,9 @@ def test_shiftadd_restatement_properties(orc):
         assert abs(p24 - exact) <= abs(exact) * 2 ** -23
         p8 = L.orc_shiftadd_mul(float(a), float(b), 8)
         assert abs(p8) <= abs(p24) and abs(p8 - exact) <= abs(exact) * 2 ** -7
+
+
+def test_attention_restatement_golden(orc, golden):
+    q, k, v, m = golden["att_q"], golden["att_k"], golden["att_v"], golden["att_mask"]
+    assert np.array_equal(orc.attention(q, k, v, None, True), golden["att_causal"])
+    assert np.array_equal(orc.attention(q, k, v, m, False), golden["att_masked"])
