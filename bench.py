@@ -397,6 +397,13 @@ def run_stream(args, world, rank, local) -> dict | None:
         fn = lambda: ext.rope_apply_(q, ctab, stab)               # noqa: E731
         bytes_, units, unit_name = 8 * q.numel(), q.numel(), "Gelem/s"
         cfg = "rac_rope_apply Q [8,32,4096,128] fp32 in place, base 1e4"
+    elif w == "attention":
+        qa, ka, va = [torch.randn((4, 32, 2048, 128), device=dev, generator=g) for _ in range(3)]
+        ao = torch.empty_like(qa)
+        fn = lambda: ext.attention(qa, ka, va, None, True, out=ao)  # noqa: E731
+        # causal: half of the 2 * B*H*T^2*hd MACs of QK^T and PV, 2 FLOP each
+        bytes_, units, unit_name = 4 * 4 * qa.numel(), 4 * 32 * 2048 * 2048 * 128, "GFLOP/s"
+        cfg = "rac_attention [4,32,2048,128] fp32 causal (the RACLlamaBlock attention core)"
     elif w == "softmax":
         x = torch.randn((32768, 4096), device=dev, generator=g) * 3
         y = torch.empty_like(x)
@@ -439,6 +446,18 @@ def run_stream(args, world, rank, local) -> dict | None:
     peaks = load_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
     ach = bytes_ / (t_local * 1e-3) / 1e9
+    if w == "attention":
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        fp32 = sms * 128 * 2 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
+        flops = units / (t_local * 1e-3) / 1e12
+        return {"metric": "rac_attention FP32 TFLOP/s (causal, algorithmic)", "value": flops * world,
+                "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": t, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "config": {"workload": cfg, "sharding": "replicas"},
+                "roofline": {"bound": "fp32", "achieved": flops, "peak": fp32, "unit": "TFLOP/s",
+                             "frac": flops / fp32, "peak_basis": "SMs x 128 lanes x 2 x sm_max_mhz",
+                             "note": "the kernel executes 1.5x the algorithmic FLOPs (scores twice)"},
+                "gpu_launches": args.steps, "clocks": clk.summary()}
     cpu = cpu_stream_baseline(w, args.iters) if (world == 1 and not args.no_cpu_baseline) else None
     return {
         "cpu_baseline": cpu,
@@ -468,7 +487,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="matmul",
-                    choices=["matmul", "rotate", "rope", "softmax", "rmsnorm", "layernorm", "llama"])
+                    choices=["matmul", "rotate", "rope", "softmax", "rmsnorm", "layernorm", "llama",
+                             "attention"])
     ap.add_argument("--size", type=int, default=4096)
     ap.add_argument("--shape", default=None, help="M,N,K for the matmul workload (e.g. 16,11008,4096)")
     ap.add_argument("--iters", type=int, default=16)
