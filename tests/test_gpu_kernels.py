@@ -225,6 +225,23 @@ def test_rotate_direction_edge_angles(cuda, orc, it):
 
 
 # ── fused attention ─────────────────────────────────────────────────────
+# Outputs are signed weighted averages of V, so many sit near zero and the
+# float32 reference is itself 4-6e-4 from the exact result under the
+# max-relative metric (normwise 3e-6): the bar is oracle.reduction_ok against
+# the float64 attention, as for LayerNorm.
+
+def _exact_attention(q, k, v, mask, causal):
+    q, k, v = [a.astype(np.float64) for a in (q, k, v)]
+    s = q @ np.swapaxes(k, -1, -2) / np.sqrt(np.float32(q.shape[-1]))
+    T = s.shape[-1]
+    if causal:
+        s = s + np.triu(np.full((T, T), -np.inf), 1)
+    if mask is not None:
+        s = s + mask.astype(np.float64)
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    return (p / p.sum(-1, keepdims=True)) @ v
+
 
 def test_attention_golden_host_abi(cuda, golden):
     """rac_attention (rac.h:330-335) with host buffers vs the reference library."""
@@ -233,10 +250,10 @@ def test_attention_golden_host_abi(cuda, golden):
     out = np.zeros_like(q)
     L.rac_attention(_p(q), _p(k), _p(v), None, 1, _p(out), *q.shape)
     _lib.check()
-    assert O.max_rel_err(out, golden["att_causal"]) <= 1e-4
+    assert O.reduction_ok(out, golden["att_causal"], _exact_attention(q, k, v, None, True))
     L.rac_attention(_p(q), _p(k), _p(v), _p(m), 0, _p(out), *q.shape)
     _lib.check()
-    assert O.max_rel_err(out, golden["att_masked"]) <= 1e-4
+    assert O.reduction_ok(out, golden["att_masked"], _exact_attention(q, k, v, m, False))
 
 
 @pytest.mark.parametrize("shape", [(2, 3, 64, 128), (1, 4, 200, 64), (2, 2, 1, 32), (1, 1, 129, 128)])
@@ -245,4 +262,5 @@ def test_attention_vs_oracle(cuda, orc, shape, causal):
     rng = np.random.default_rng(sum(shape) + causal)
     q, k, v = [rng.standard_normal(shape).astype(np.float32) for _ in range(3)]
     got = ext.attention(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, bool(causal)).cpu().numpy()
-    assert O.max_rel_err(got, orc.attention(q, k, v, None, causal)) <= 1e-4
+    assert O.reduction_ok(got, orc.attention(q, k, v, None, causal),
+                          _exact_attention(q, k, v, None, causal))
