@@ -401,8 +401,8 @@ def run_stream(args, world, rank, local) -> dict | None:
         qa, ka, va = [torch.randn((4, 32, 2048, 128), device=dev, generator=g) for _ in range(3)]
         ao = torch.empty_like(qa)
         fn = lambda: ext.attention(qa, ka, va, None, True, out=ao)  # noqa: E731
-        # causal: half of the 2 * B*H*T^2*hd MACs of QK^T and PV, 2 FLOP each
-        bytes_, units, unit_name = 4 * 4 * qa.numel(), 4 * 32 * 2048 * 2048 * 128, "GFLOP/s"
+        # causal: QK^T and PV each B*H*T*(T/2)*hd MACs, 2 FLOP per MAC
+        bytes_, units, unit_name = 4 * 4 * qa.numel(), 2 * 4 * 32 * 2048 * 2048 * 128, "TFLOP/s"
         cfg = "rac_attention [4,32,2048,128] fp32 causal (the RACLlamaBlock attention core)"
     elif w == "softmax":
         x = torch.randn((32768, 4096), device=dev, generator=g) * 3
