@@ -7,14 +7,14 @@
 //
 // One CTA owns 64 query rows of one (batch, head) and streams the keys in
 // 64-row tiles through shared memory; the [seq, seq] score matrix never
-// exists in HBM.  Pass 1 recomputes the scores only for the exact row max
-// (max is order independent); pass 2 recomputes them, forms e = expf(s - max),
-// the row sum, and accumulates O += e * V key by key in ascending order, then
-// scales by 1/sum.  So the scores are bit-identical to the reference and the
-// output differs from it only by expf's last bit and the sum's association
-// (the reference multiplies by 1/sum before accumulating).  Recomputing the
-// scores (instead of online rescaling) keeps the output deterministic and
-// that close to the reference for 1.5x the FLOPs of a single pass.
+// exists in HBM.  Scores are accumulated over d in ascending order exactly as
+// the reference does (bit-identical scores); the softmax is online -- a
+// running row max with rescaling of the partial sum and of O -- and O
+// accumulates e * V key by key in ascending order, scaled by 1/sum at the
+// end.  The output differs from the reference by expf's last bit, the
+// rescaling roundings and the sum's association (the reference multiplies by
+// 1/sum before accumulating): within the reference's own distance from the
+// exact result.  Deterministic (fixed tile order).
 //
 // 128 threads: for the 64x64 score tile a thread owns rows 4*rg..4*rg+3 and
 // columns cg + 8j (j < 8); for the 64 x HD output it owns the same rows and
@@ -119,25 +119,10 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
 
     load_tile<HD>(Qs, qh, t0, seq);
 
-    // Pass 1: exact row max.
+    // One pass with the running (online) row max m: per key tile,
+    // m' = max(m, tile max), alpha = expf(m - m'), e = expf(s - m'),
+    // l = l * alpha + sum e, O = O * alpha + e V (keys ascending).
     float mrow[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    for (int kb = 0; kb < nkb; ++kb) {
-        __syncthreads();
-        load_tile<HD>(KVs, kh, kb * kAttBK, seq);
-        __syncthreads();
-        float sc[4][8];
-        tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) mrow[i] = fmaxf(mrow[i], sc[i][j]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) mrow[i] = fmaxf(mrow[i], __shfl_xor_sync(0xffffffffu, mrow[i], o));
-
-    // Pass 2: e = expf(s - max), row sums, O += e V in key order.
     float lsum[4] = {0.f, 0.f, 0.f, 0.f};
     float4 o[4][CG];
 #pragma unroll
@@ -151,13 +136,29 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         float sc[4][8];
         tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i) {
+            float tm = sc[i][0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) tm = fmaxf(tm, sc[i][j]);
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+            const float mn = fmaxf(mrow[i], tm);
+            // Rows with no finite score yet contribute nothing (their e = 0).
+            const float alpha = (mn == -INFINITY) ? 1.0f : expf(__fsub_rn(mrow[i], mn));
+            mrow[i] = mn;
+            lsum[i] = __fmul_rn(lsum[i], alpha);
+#pragma unroll
+            for (int g = 0; g < CG; ++g) {
+                o[i][g].x = __fmul_rn(o[i][g].x, alpha); o[i][g].y = __fmul_rn(o[i][g].y, alpha);
+                o[i][g].z = __fmul_rn(o[i][g].z, alpha); o[i][g].w = __fmul_rn(o[i][g].w, alpha);
+            }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float e = expf(__fsub_rn(sc[i][j], mrow[i]));
+                const float e = (mn == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[i][j], mn));
                 lsum[i] = __fadd_rn(lsum[i], e);
                 Ps[(rg * 4 + i) * PLD + cg + 8 * j] = e;
             }
+        }
         __syncthreads();
         load_tile<HD>(KVs, vh, kb * kAttBK, seq);
         __syncthreads();
@@ -187,7 +188,10 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     for (int i = 0; i < 4; ++i) {
         const int t = t0 + rg * 4 + i;
         if (t >= seq) continue;
-        const float inv = lsum[i] > 0.0f ? __fdiv_rn(1.0f, lsum[i]) : 0.0f;
+        // A row whose scores are all -inf gives NaN, as in the reference
+        // (expf(-inf - -inf) there); otherwise inv = 1/sum (sum > 0).
+        const float inv = mrow[i] == -INFINITY ? __int_as_float(0x7fc00000)
+                        : (lsum[i] > 0.0f ? __fdiv_rn(1.0f, lsum[i]) : 0.0f);
 #pragma unroll
         for (int g = 0; g < CG; ++g) {
             const float4 r = o[i][g];

@@ -264,3 +264,20 @@ def test_attention_vs_oracle(cuda, orc, shape, causal):
     got = ext.attention(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, bool(causal)).cpu().numpy()
     assert O.reduction_ok(got, orc.attention(q, k, v, None, causal),
                           _exact_attention(q, k, v, None, causal))
+
+
+def test_attention_masked_tiles_and_dead_rows(cuda, orc):
+    """Rows whose first 64-key tile is fully masked must still match; a row with
+    every score -inf is NaN in the reference (expf(-inf - -inf)) and here."""
+    rng = np.random.default_rng(21)
+    q, k, v = [rng.standard_normal((1, 2, 150, 64)).astype(np.float32) for _ in range(3)]
+    mask = np.zeros((150, 150), np.float32)
+    mask[:20, :64] = -np.inf
+    mask[30, :] = -np.inf
+    got = ext.attention(_t(q, cuda), _t(k, cuda), _t(v, cuda), _t(mask, cuda), False).cpu().numpy()
+    want = orc.attention(q, k, v, mask, 0)
+    assert np.isnan(want[:, :, 30]).all() and np.isnan(got[:, :, 30]).all()
+    keep = np.ones(150, bool)
+    keep[30] = False
+    ex = _exact_attention(q, k, v, mask, False)
+    assert O.reduction_ok(got[:, :, keep], want[:, :, keep], ex[:, :, keep])
