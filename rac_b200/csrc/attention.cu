@@ -16,7 +16,7 @@
 // 1/sum before accumulating): within the reference's own distance from the
 // exact result.  Deterministic (fixed tile order).
 //
-// 128 threads: for the 64x64 score tile a thread owns rows 4*rg..4*rg+3 and
+// 128 threads: for the 64x64 score tile a thread owns rows rg + 16i (i < 4) and
 // columns cg + 8j (j < 8); for the 64 x HD output it owns the same rows and
 // HD/8 columns in float4 groups.  Shared rows are padded by 4 floats so that
 // the float4 reads of K, V and P are bank-conflict free.
@@ -65,7 +65,7 @@ __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, 
     for (int d = 0; d < HD; d += 4) {
         float4 q[4], k[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg * 4 + i) * LD + d);
+        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * LD + d);
 #pragma unroll
         for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * LD + d);
 #pragma unroll
@@ -82,7 +82,7 @@ __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, 
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int t = t0 + rg * 4 + i;
+        const int t = t0 + rg + 16 * i;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int s = s0 + cg + 8 * j;
@@ -156,7 +156,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
             for (int j = 0; j < 8; ++j) {
                 const float e = (mn == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[i][j], mn));
                 lsum[i] = __fadd_rn(lsum[i], e);
-                Ps[(rg * 4 + i) * PLD + cg + 8 * j] = e;
+                Ps[(rg + 16 * i) * PLD + cg + 8 * j] = e;
             }
         }
         __syncthreads();
@@ -166,7 +166,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         for (int s = 0; s < kmax; ++s) {
             float p[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = Ps[(rg * 4 + i) * PLD + s];
+            for (int i = 0; i < 4; ++i) p[i] = Ps[(rg + 16 * i) * PLD + s];
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
                 const float4 vv = *reinterpret_cast<const float4*>(KVs + s * LD + cg * 4 + 32 * g);
@@ -186,7 +186,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         for (int off = 1; off < 8; off <<= 1) lsum[i] = __fadd_rn(lsum[i], __shfl_xor_sync(0xffffffffu, lsum[i], off));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int t = t0 + rg * 4 + i;
+        const int t = t0 + rg + 16 * i;
         if (t >= seq) continue;
         // A row whose scores are all -inf gives NaN, as in the reference
         // (expf(-inf - -inf) there); otherwise inv = 1/sum (sum > 0).
