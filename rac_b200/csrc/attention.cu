@@ -16,9 +16,9 @@
 // 1/sum before accumulating): within the reference's own distance from the
 // exact result.  Deterministic (fixed tile order).
 //
-// 256 threads: for the 64x64 score tile a thread owns rows rg + 32i (i < 2) and
+// 128 threads: for the 64x64 score tile a thread owns rows rg + 16i (i < 4) and
 // columns cg + 8j (j < 8); for the 64 x HD output it owns the same rows and
-// HD/8 columns in float4 groups (about 128 registers: two CTAs, 16 warps per SM).  Shared rows are padded by 4 floats so that
+// HD/8 columns in float4 groups.  Shared rows are padded by 4 floats so that
 // the float4 reads of K, V and P are bank-conflict free.
 #include <cmath>
 
@@ -27,9 +27,7 @@
 
 namespace racb {
 
-constexpr int kAttBQ = 64, kAttBK = 64, kAttThreads = 256;
-// Rows of the 64-row tiles per thread: 256 threads = 32 row groups x 8 column groups.
-constexpr int kAttRG = kAttThreads / 8, kAttRPT = kAttBQ / kAttRG;
+constexpr int kAttBQ = 64, kAttBK = 64, kAttThreads = 128;
 
 template <int HD>
 struct AttSmem {
@@ -54,24 +52,24 @@ __device__ __forceinline__ void load_tile(float* dst, const float* __restrict__ 
 // Scores of this thread's 4 x 8 block for the key tile in Ks, after scale,
 // causal and mask (keys beyond seq -> -inf).
 template <int HD>
-__device__ __forceinline__ void tile_scores(float (&sc)[kAttRPT][8], const float* Qs, const float* Ks,
+__device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, const float* Ks,
                                             int t0, int s0, int seq, float scale, int causal,
                                             const float* __restrict__ mask) {
     constexpr int LD = AttSmem<HD>::LD;
     const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
 #pragma unroll
-    for (int i = 0; i < kAttRPT; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) sc[i][j] = 0.0f;
 #pragma unroll 4
     for (int d = 0; d < HD; d += 4) {
-        float4 q[kAttRPT], k[8];
+        float4 q[4], k[8];
 #pragma unroll
-        for (int i = 0; i < kAttRPT; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + kAttRG * i) * LD + d);
+        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * LD + d);
 #pragma unroll
         for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * LD + d);
 #pragma unroll
-        for (int i = 0; i < kAttRPT; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float a = sc[i][j];
@@ -83,8 +81,8 @@ __device__ __forceinline__ void tile_scores(float (&sc)[kAttRPT][8], const float
             }
     }
 #pragma unroll
-    for (int i = 0; i < kAttRPT; ++i) {
-        const int t = t0 + rg + kAttRG * i;
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + rg + 16 * i;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int s = s0 + cg + 8 * j;
@@ -124,22 +122,21 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     // One pass with the running (online) row max m: per key tile,
     // m' = max(m, tile max), alpha = expf(m - m'), e = expf(s - m'),
     // l = l * alpha + sum e, O = O * alpha + e V (keys ascending).
-    float mrow[kAttRPT], lsum[kAttRPT];
+    float mrow[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+    float4 o[4][CG];
 #pragma unroll
-    for (int i = 0; i < kAttRPT; ++i) { mrow[i] = -INFINITY; lsum[i] = 0.0f; }
-    float4 o[kAttRPT][CG];
-#pragma unroll
-    for (int i = 0; i < kAttRPT; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int g = 0; g < CG; ++g) o[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int kb = 0; kb < nkb; ++kb) {
         __syncthreads();
         load_tile<HD>(KVs, kh, kb * kAttBK, seq);
         __syncthreads();
-        float sc[kAttRPT][8];
+        float sc[4][8];
         tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
 #pragma unroll
-        for (int i = 0; i < kAttRPT; ++i) {
+        for (int i = 0; i < 4; ++i) {
             float tm = sc[i][0];
 #pragma unroll
             for (int j = 1; j < 8; ++j) tm = fmaxf(tm, sc[i][j]);
@@ -159,7 +156,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
             for (int j = 0; j < 8; ++j) {
                 const float e = (mn == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[i][j], mn));
                 lsum[i] = __fadd_rn(lsum[i], e);
-                Ps[(rg + kAttRG * i) * PLD + cg + 8 * j] = e;
+                Ps[(rg + 16 * i) * PLD + cg + 8 * j] = e;
             }
         }
         __syncthreads();
@@ -167,14 +164,14 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         __syncthreads();
         const int kmax = min(kAttBK, seq - kb * kAttBK);
         for (int s = 0; s < kmax; ++s) {
-            float p[kAttRPT];
+            float p[4];
 #pragma unroll
-            for (int i = 0; i < kAttRPT; ++i) p[i] = Ps[(rg + kAttRG * i) * PLD + s];
+            for (int i = 0; i < 4; ++i) p[i] = Ps[(rg + 16 * i) * PLD + s];
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
                 const float4 vv = *reinterpret_cast<const float4*>(KVs + s * LD + cg * 4 + 32 * g);
 #pragma unroll
-                for (int i = 0; i < kAttRPT; ++i) {
+                for (int i = 0; i < 4; ++i) {
                     o[i][g].x = __fmaf_rn(p[i], vv.x, o[i][g].x);
                     o[i][g].y = __fmaf_rn(p[i], vv.y, o[i][g].y);
                     o[i][g].z = __fmaf_rn(p[i], vv.z, o[i][g].z);
@@ -184,12 +181,12 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         }
     }
 #pragma unroll
-    for (int i = 0; i < kAttRPT; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int off = 1; off < 8; off <<= 1) lsum[i] = __fadd_rn(lsum[i], __shfl_xor_sync(0xffffffffu, lsum[i], off));
 #pragma unroll
-    for (int i = 0; i < kAttRPT; ++i) {
-        const int t = t0 + rg + kAttRG * i;
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + rg + 16 * i;
         if (t >= seq) continue;
         // A row whose scores are all -inf gives NaN, as in the reference
         // (expf(-inf - -inf) there); otherwise inv = 1/sum (sum > 0).
