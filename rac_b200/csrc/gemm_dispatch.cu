@@ -1,4 +1,6 @@
 // gemm_dispatch.cu -- picks the GEMM kernel instance for a call.
+#include <cstdlib>
+#include <cudaTypedefs.h>
 #include <mutex>
 
 #include "gemm_kernel.cuh"
@@ -17,6 +19,78 @@ E4(kShiftAdd, 0, kNN) E4(kShiftAdd, 0, kNT) E4(kShiftAdd, 0, kTN)
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 2, true) RACB_GEMM_EXTERN(kCordic, ITERS, kNN, 4, true) \
     RACB_GEMM_EXTERN(kCordic, ITERS, kNT, 4, true)
 E2(8) E2(16) E2(24)
+#define ET(ITERS) RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNN, 1) RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNT, 1) \
+    RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNN, 2) RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNT, 2) \
+    RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNN, 3) RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNT, 3) \
+    RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNN, 4) RACB_GEMM_EXTERN_TMA(kCordic, ITERS, kNT, 4)
+ET(8) ET(16) ET(24)
+
+template <int ITERS, int LAYOUT>
+static int launch_tma_tile(const GemmParams& p, int v, cudaStream_t s) {
+    switch (v) {
+        case 2: return launch_inst<kCordic, ITERS, LAYOUT, 2, true, true>(p, s);
+        case 3: return launch_inst<kCordic, ITERS, LAYOUT, 3, true, true>(p, s);
+        case 4: return launch_inst<kCordic, ITERS, LAYOUT, 4, true, true>(p, s);
+        default: return launch_inst<kCordic, ITERS, LAYOUT, 1, true, true>(p, s);
+    }
+}
+
+template <int ITERS>
+static int pick_fixed_tma(const GemmParams& p, int layout, int v, cudaStream_t s) {
+    return layout == kNN ? launch_tma_tile<ITERS, kNN>(p, v, s) : launch_tma_tile<ITERS, kNT>(p, v, s);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+static bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                      long long ld, uint32_t box_inner, uint32_t box_outer) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 4) & 15)) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK) {
+    // Boxes start at k multiples of BK and m / n multiples of BM / BN, so the
+    // innermost coordinate of every copy is a multiple of 8 floats (32 B).
+    const bool a_ok = layout == kTN ? encode_2d(&p.tmA, p.A, p.M, p.K, p.lda, BM, BK)
+                                    : encode_2d(&p.tmA, p.A, p.K, p.M, p.lda, BK, BM);
+    const bool b_ok = layout == kNT ? encode_2d(&p.tmB, p.B, p.K, p.N, p.ldb, BK, BN)
+                                    : encode_2d(&p.tmB, p.B, p.N, p.K, p.ldb, BN, BK);
+    return a_ok && b_ok;
+}
+
+// TMA staging for the fixed-n CORDIC kernels: variant bit 0x100 forces it,
+// 0x200 forces the register-staged loader, otherwise env RAC_GEMM_TMA (1/0).
+static bool use_tma(int variant) {
+    if (variant & 0x100) return true;
+    if (variant & 0x200) return false;
+    static int env = -1;
+    if (env < 0) {
+        const char* e = std::getenv("RAC_GEMM_TMA");
+        env = (e && e[0] == '0') ? 0 : 1;
+    }
+    return env == 1;
+}
 
 template <int MODE, int ITERS, int LAYOUT>
 static int pick_tile(const GemmParams& p, int v, bool vec, cudaStream_t s) {
@@ -151,7 +225,7 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
     if (!p_in.A || !p_in.B || !p_in.C) return kErrNullPtr;
     if (layout < kNN || layout > kTN) return kErrUnsupported;
     if (p_in.beta != 0.0f && !p_in.Cin) return kErrNullPtr;
-    const int S = splitk_count(p_in, layout, mode, variant);
+    const int S = splitk_count(p_in, layout, mode, variant & 0xff);
     if (S <= 1) {
         GemmParams p = p_in;
         p.ws = nullptr; p.splits = 1; p.kchunk = 0;
@@ -177,7 +251,12 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
 // the caller: ws == nullptr means no split).
 int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
     GemmParams p = p_in;
+    const bool tma = use_tma(variant);
+    variant &= 0xff;
     int v = tile_variant(p, variant);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    p.err = device_error_word(dev);
     // Vector loads need 16-byte aligned bases, leading dims that are
     // multiples of 4 and contiguous extents that are multiples of 4.
     const int a_contig = (layout == kTN) ? p.M : p.K;
@@ -195,6 +274,14 @@ int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, 
     for (int i = 0; i < 24; ++i) p.coef[i] = gemm_coef(i);
     const bool fixed = vec && layout != kTN && (p.iters == 8 || p.iters == 16 || p.iters == 24);
     if ((v == 2 || v == 4) && !fixed) v = 1;   // tiles 2 and 4 exist for the fixed-n kernels only
+    if (fixed && tma) {
+        GemmParams q = p;
+        if (make_tensor_maps(q, layout, 64, 64, 8)) {        // operands meet the TMA rules
+            if (p.iters == 8) return pick_fixed_tma<8>(p, layout, v, s);
+            if (p.iters == 16) return pick_fixed_tma<16>(p, layout, v, s);
+            return pick_fixed_tma<24>(p, layout, v, s);
+        }
+    }
     if (fixed && p.iters == 8) return pick_fixed<8>(p, layout, v, s);
     if (fixed && p.iters == 16) return pick_fixed<16>(p, layout, v, s);
     if (fixed && p.iters == 24) return pick_fixed<24>(p, layout, v, s);

@@ -95,14 +95,55 @@ struct TileLoader {
     }
 };
 
+// ── TMA staging (cp.async.bulk.tensor, no multicast) ──────────────────────
+// Tensor maps are built on the host (gemm_dispatch.cu) and passed inside the
+// __grid_constant__ parameters.  One elected thread issues the copies of a
+// stage; every thread waits on that stage's mbarrier with a bounded loop.
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+                    "r"(smem_u32(bar)) : "memory");
+}
+// Upper bound on the polls of one stage barrier: a copy that never lands sets
+// bit 1 of the device error word instead of hanging the kernel.
+constexpr uint32_t kTmaWaitLimit = 1u << 22;
+
 template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC,
-          int MINB = 1>
+          int MINB = 1, bool TMA = false>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN), MINB)
 k_gemm(const __grid_constant__ GemmParams p) {
     constexpr int TX = BN / TN, TY = BM / TM, NT = TX * TY;
-    // Tiles are k-major in shared memory: row kk holds BM (BN) operands.
-    __shared__ __align__(16) float As[2][BK * BM];
-    __shared__ __align__(16) float Bs[2][BK * BN];
+    constexpr int STAGES = TMA ? 4 : 2;
+    // A: NN/NT store A[M,K] (k contiguous); TN stores A[K,M].
+    // B: NN/TN store B[K,N] (n contiguous); NT stores B[N,K].
+    constexpr bool A_KCOLS = (LAYOUT != kTN);
+    constexpr bool B_KCOLS = (LAYOUT == kNT);
+    // Shared-memory layout of a stage.  The register-staged path transposes
+    // into k-major rows; TMA copies the box as it lies in global memory, so
+    // an operand whose global rows run along k lands m-/n-major.
+    constexpr bool A_KMAJOR = TMA ? !A_KCOLS : true;
+    constexpr bool B_KMAJOR = TMA ? !B_KCOLS : true;
+    __shared__ __align__(128) float As[STAGES][BK * BM];
+    __shared__ __align__(128) float Bs[STAGES][BK * BN];
+    __shared__ __align__(8) uint64_t full_bar[TMA ? STAGES : 1];
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
@@ -110,24 +151,6 @@ k_gemm(const __grid_constant__ GemmParams p) {
     const int kbeg = p.ws ? blockIdx.z * p.kchunk : 0;
     const int kend = p.ws ? min(p.K, kbeg + p.kchunk) : p.K;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;   // m tiles on x (2^31 limit)
-
-    // A: NN/NT store A[M,K] (k contiguous); TN stores A[K,M].
-    // B: NN/TN store B[K,N] (n contiguous); NT stores B[N,K].
-    constexpr bool A_KCOLS = (LAYOUT != kTN);
-    constexpr bool B_KCOLS = (LAYOUT == kNT);
-    TileLoader<A_KCOLS ? BM : BK, A_KCOLS ? BK : BM, NT, VEC> la;
-    TileLoader<B_KCOLS ? BN : BK, B_KCOLS ? BK : BN, NT, VEC> lb;
-
-    auto load_tiles = [&](int k0) {
-        if constexpr (A_KCOLS) la.load(p.A, p.lda, m0, k0, p.M, kend, tid);
-        else                   la.load(p.A, p.lda, k0, m0, kend, p.M, tid);
-        if constexpr (B_KCOLS) lb.load(p.B, p.ldb, n0, k0, p.N, kend, tid);
-        else                   lb.load(p.B, p.ldb, k0, n0, kend, p.N, tid);
-    };
-    auto store_tiles = [&](int buf) {
-        la.template store<A_KCOLS, BM>(As[buf], tid);
-        lb.template store<B_KCOLS, BN>(Bs[buf], tid);
-    };
 
     float acc[TM][TN];
 #pragma unroll
@@ -138,67 +161,122 @@ k_gemm(const __grid_constant__ GemmParams p) {
     const float k_inv = p.k_inv;
     const int ktiles = (kend - kbeg + BK - 1) / BK;
 
-    load_tiles(kbeg);
-    store_tiles(0);
-    __syncthreads();
-
-    for (int kt = 0; kt < ktiles; ++kt) {
-        const int buf = kt & 1;
-        if (kt + 1 < ktiles) load_tiles(kbeg + (kt + 1) * BK);   // in flight during compute
-
-        const float* __restrict__ Asb = As[buf];
-        const float* __restrict__ Bsb = Bs[buf];
-#pragma unroll 1
-        for (int kk = 0; kk < BK; ++kk) {
-            float a[TM], b[TN];
+    // One k-step of the register tile from stage buffers Asb / Bsb.
+    auto mac_step = [&](const float* __restrict__ Asb, const float* __restrict__ Bsb, int kk) {
+        float a[TM], b[TN];
+        if constexpr (A_KMAJOR) {
 #pragma unroll
             for (int i = 0; i < TM; i += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(&Asb[kk * BM + ty * TM + i]);
                 a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
             }
+        } else {
+#pragma unroll
+            for (int i = 0; i < TM; ++i) a[i] = Asb[(ty * TM + i) * BK + kk];
+        }
+        if constexpr (B_KMAJOR) {
 #pragma unroll
             for (int j = 0; j < TN; j += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(&Bsb[kk * BN + tx * TN + j]);
                 b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
             }
-            if constexpr (MODE == kFast) {
+        } else {
 #pragma unroll
-                for (int i = 0; i < TM; ++i)
+            for (int j = 0; j < TN; ++j) b[j] = Bsb[(tx * TN + j) * BK + kk];
+        }
+        if constexpr (MODE == kFast) {
 #pragma unroll
-                    for (int j = 0; j < TN; ++j)
-                        acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
-            } else if constexpr (MODE == kShiftAdd) {
-                // rac_fma_iters SHIFTADD (rac_kernels.hip:217-218): acc + prod.
+            for (int i = 0; i < TM; ++i)
 #pragma unroll
-                for (int i = 0; i < TM; ++i)
+                for (int j = 0; j < TN; ++j)
+                    acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+        } else if constexpr (MODE == kShiftAdd) {
+            // rac_fma_iters SHIFTADD (rac_kernels.hip:217-218): acc + prod.
 #pragma unroll
-                    for (int j = 0; j < TN; ++j)
-                        acc[i][j] = __fadd_rn(acc[i][j], shiftadd_mul(a[i], b[j], p.iters));
-            } else {
-                uint32_t sgn[TN];
-                float mag[TN];
+            for (int i = 0; i < TM; ++i)
 #pragma unroll
-                for (int j = 0; j < TN; ++j) {
-                    sgn[j] = __float_as_uint(b[j]) & 0x80000000u;
-                    mag[j] = __uint_as_float(__float_as_uint(b[j]) & 0x7FFFFFFFu);
-                }
+                for (int j = 0; j < TN; ++j)
+                    acc[i][j] = __fadd_rn(acc[i][j], shiftadd_mul(a[i], b[j], p.iters));
+        } else {
+            uint32_t sgn[TN];
+            float mag[TN];
 #pragma unroll
-                for (int j = 0; j < TN; ++j) {
+            for (int j = 0; j < TN; ++j) {
+                sgn[j] = __float_as_uint(b[j]) & 0x80000000u;
+                mag[j] = __uint_as_float(__float_as_uint(b[j]) & 0x7FFFFFFFu);
+            }
 #pragma unroll
-                    for (int i = 0; i < TM; ++i) {
-                        const float sa = __uint_as_float(__float_as_uint(a[i]) ^ sgn[j]);
-                        float x;
-                        if constexpr (ITERS > 0) x = gemm_cordic_x<ITERS>(sa);
-                        else                     x = gemm_cordic_x_rt(sa, p.iters, p.coef);
-                        acc[i][j] = __fmaf_rn(__fmul_rn(x, k_inv), mag[j], acc[i][j]);
-                    }
+            for (int j = 0; j < TN; ++j) {
+#pragma unroll
+                for (int i = 0; i < TM; ++i) {
+                    const float sa = __uint_as_float(__float_as_uint(a[i]) ^ sgn[j]);
+                    float x;
+                    if constexpr (ITERS > 0) x = gemm_cordic_x<ITERS>(sa);
+                    else                     x = gemm_cordic_x_rt(sa, p.iters, p.coef);
+                    acc[i][j] = __fmaf_rn(__fmul_rn(x, k_inv), mag[j], acc[i][j]);
                 }
             }
         }
-        if (kt + 1 < ktiles) {
-            store_tiles(buf ^ 1);
+    };
+
+    if constexpr (TMA) {
+        constexpr uint32_t kStageBytes = sizeof(float) * (BM + BN) * BK;
+        auto issue = [&](int stage, int k0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(&full_bar[stage], kStageBytes);
+            if constexpr (A_KCOLS) tma_load_2d(As[stage], &p.tmA, k0, m0, &full_bar[stage]);
+            else                   tma_load_2d(As[stage], &p.tmA, m0, k0, &full_bar[stage]);
+            if constexpr (B_KCOLS) tma_load_2d(Bs[stage], &p.tmB, k0, n0, &full_bar[stage]);
+            else                   tma_load_2d(Bs[stage], &p.tmB, n0, k0, &full_bar[stage]);
+        };
+        if (tid == 0) {
+#pragma unroll
+            for (int st = 0; st < STAGES; ++st) mbar_init(&full_bar[st], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         __syncthreads();
+        if (tid == 0)
+            for (int st = 0; st < STAGES && st < ktiles; ++st) issue(st, kbeg + st * BK);
+        bool timed_out = false;
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int st = kt % STAGES;
+            const uint32_t parity = (kt / STAGES) & 1u;
+            if (!timed_out) {
+                uint32_t polls = 0;
+                while (!mbar_try_wait(&full_bar[st], parity)) {
+                    if (++polls >= kTmaWaitLimit) { timed_out = true; break; }
+                }
+            }
+#pragma unroll 1
+            for (int kk = 0; kk < BK; ++kk) mac_step(As[st], Bs[st], kk);
+            __syncthreads();                       // every thread is done with stage st
+            if (tid == 0 && kt + STAGES < ktiles) issue(st, kbeg + (kt + STAGES) * BK);
+        }
+        if (timed_out && p.err) atomicOr(p.err, 2u);
+    } else {
+        TileLoader<A_KCOLS ? BM : BK, A_KCOLS ? BK : BM, NT, VEC> la;
+        TileLoader<B_KCOLS ? BN : BK, B_KCOLS ? BK : BN, NT, VEC> lb;
+        auto load_tiles = [&](int k0) {
+            if constexpr (A_KCOLS) la.load(p.A, p.lda, m0, k0, p.M, kend, tid);
+            else                   la.load(p.A, p.lda, k0, m0, kend, p.M, tid);
+            if constexpr (B_KCOLS) lb.load(p.B, p.ldb, n0, k0, p.N, kend, tid);
+            else                   lb.load(p.B, p.ldb, k0, n0, kend, p.N, tid);
+        };
+        auto store_tiles = [&](int buf) {
+            la.template store<A_KCOLS, BM>(As[buf], tid);
+            lb.template store<B_KCOLS, BN>(Bs[buf], tid);
+        };
+        load_tiles(kbeg);
+        store_tiles(0);
+        __syncthreads();
+        for (int kt = 0; kt < ktiles; ++kt) {
+            const int buf = kt & 1;
+            if (kt + 1 < ktiles) load_tiles(kbeg + (kt + 1) * BK);   // in flight during compute
+#pragma unroll 1
+            for (int kk = 0; kk < BK; ++kk) mac_step(As[buf], Bs[buf], kk);
+            if (kt + 1 < ktiles) store_tiles(buf ^ 1);
+            __syncthreads();
+        }
     }
 
     if (p.ws) {   // split-K partial: raw sums, the reduction applies the epilogue
@@ -249,13 +327,19 @@ template <> struct TileCfg<3> { static constexpr int BM = 16, BN = 128, BK = 8, 
 // 4: 32x64, 4x4 per thread: finer tiles for narrow shards (4096x512 per GPU).
 template <> struct TileCfg<4> { static constexpr int BM = 32, BN = 64, BK = 8, TM = 4, TN = 4, MINB = 8; };
 
-template <int MODE, int ITERS, int LAYOUT, int V, bool VEC>
-int launch_inst(const GemmParams& p, cudaStream_t s) {
+template <int MODE, int ITERS, int LAYOUT, int V, bool VEC, bool TMA = false>
+int launch_inst(const GemmParams& p_in, cudaStream_t s) {
     using T = TileCfg<V>;
     constexpr int NT = (T::BM / T::TM) * (T::BN / T::TN);
-    dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN, p.ws ? p.splits : 1);
+    dim3 grid((p_in.M + T::BM - 1) / T::BM, (p_in.N + T::BN - 1) / T::BN, p_in.ws ? p_in.splits : 1);
     if (grid.y > 65535) return kErrInvalidDim;
-    k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC, T::MINB><<<grid, NT, 0, s>>>(p);
+    if constexpr (TMA) {
+        GemmParams p = p_in;
+        if (!make_tensor_maps(p, LAYOUT, T::BM, T::BN, T::BK)) return kErrUnsupported;
+        k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC, T::MINB, true><<<grid, NT, 0, s>>>(p);
+    } else {
+        k_gemm<MODE, ITERS, LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, VEC, T::MINB><<<grid, NT, 0, s>>>(p_in);
+    }
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -265,5 +349,9 @@ int launch_inst(const GemmParams& p, cudaStream_t s) {
     template int launch_inst<MODE, ITERS, LAYOUT, V, VEC>(const GemmParams&, cudaStream_t);
 #define RACB_GEMM_EXTERN(MODE, ITERS, LAYOUT, V, VEC) \
     extern template int launch_inst<MODE, ITERS, LAYOUT, V, VEC>(const GemmParams&, cudaStream_t);
+#define RACB_GEMM_INST_TMA(MODE, ITERS, LAYOUT, V) \
+    template int launch_inst<MODE, ITERS, LAYOUT, V, true, true>(const GemmParams&, cudaStream_t);
+#define RACB_GEMM_EXTERN_TMA(MODE, ITERS, LAYOUT, V) \
+    extern template int launch_inst<MODE, ITERS, LAYOUT, V, true, true>(const GemmParams&, cudaStream_t);
 
 }  // namespace racb

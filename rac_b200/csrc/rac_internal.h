@@ -2,6 +2,7 @@
 // Nothing here is part of the public C ABI (that is include/rac.h and
 // include/rac_b200.h).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -42,7 +43,17 @@ struct GemmParams {
     float* ws;
     int kchunk;
     int splits;
+    // TMA-staged kernels: 2-D tensor maps of A and B (built by make_tensor_maps)
+    // and the device error word their bounded waits report to.
+    alignas(64) CUtensorMap tmA;
+    alignas(64) CUtensorMap tmB;
+    unsigned int* err;
 };
+
+// Fills p.tmA / p.tmB for a TMA-staged launch with a BM x BN x BK tile.
+// Returns false when the operands do not meet the TMA rules (16-byte aligned
+// bases and leading dimensions) or the driver entry point is unavailable.
+bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK);
 
 // launch_gemm without the split-K decision: launches the tile kernel for p
 // as given (p.ws == nullptr: whole K per CTA).

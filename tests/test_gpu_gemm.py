@@ -210,3 +210,35 @@ def test_shiftadd_edge_values(cuda, orc):
     for it in (1, 8, 24):
         got = ext.gemm(_t(A, cuda), _t(B, cuda), LAYOUT_NN, it, 2).cpu().numpy()
         assert np.array_equal(got, orc.gemm(A, B, "nn", 2, it))
+
+
+TMA, REGS = 0x100, 0x200      # variant bits: force the TMA / register-staged loader
+
+
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("layout", ["nn", "nt"])
+@pytest.mark.parametrize("shape", [(200, 328, 260), (16, 1000, 520), (129, 65, 36)])
+def test_tma_staging_bitexact(cuda, orc, variant, layout, shape):
+    """cp.async.bulk.tensor staging (4-stage mbarrier pipeline) computes the same
+    bits as the register-staged loader and the CPU restatement, including
+    out-of-range boxes (M, N not multiples of the tile; K tail)."""
+    M, N, K = shape
+    A, B = _operands(M, N, K, layout, variant + M)
+    dA, dB = _t(A, cuda), _t(B, cuda)
+    got = ext.gemm(dA, dB, LAY[layout], 16, 1, variant=TMA | variant).cpu().numpy()
+    ref = ext.gemm(dA, dB, LAY[layout], 16, 1, variant=REGS | variant).cpu().numpy()
+    assert np.array_equal(got, ref)
+    assert np.array_equal(got, orc.gemm(A, B, layout, 1, 16))
+    ext.check_device_errors()
+
+
+def test_tma_staging_splitk_and_strided(cuda, orc):
+    M, N, K = 64, 192, 2048
+    A, B = _operands(M, N, K, "nn", 5)
+    big = torch.zeros((M, K + 16), device=cuda)
+    big[:, 4:4 + K] = _t(A, cuda)                      # leading dim K+16, base +16 B
+    got = ext.gemm(big[:, 4:4 + K], _t(B, cuda), LAYOUT_NN, 8, 1, variant=TMA | 13).cpu().numpy()
+    ref = ext.gemm(_t(A, cuda), _t(B, cuda), LAYOUT_NN, 8, 1, variant=REGS | 13).cpu().numpy()
+    assert np.array_equal(got, ref)
+    assert _normwise(got, orc.gemm(A, B, "nn", 1, 8)) <= NORM_TOL
+    ext.check_device_errors()
