@@ -90,25 +90,39 @@ __host__ __device__ constexpr float gemm_coef(int i) {
 // One CORDIC MAC of rac_fma_cordic (rac_kernels.hip:176-185) with the fold
 // already applied: the vector entering the iterations is (sa, 0) where
 // sa = a with b's sign bit xor-ed in (the fold negates it when b < 0).
-// Iteration 0 has scale 1 and y = 0, so it maps (sa, 0) to (sa, sa) exactly;
-// iterations 1..ITERS-1 are x' = x - c_i*y, y' = y + c_i*x with c_i = d_i*2^-i
-// (one rounding each: c_i*y is exact).  Only x of the last iteration is used.
-// Returns x_n (before the 1/K(n) compensation).
+// Iteration i is x' = x - c_i*y, y' = y + c_i*x with c_i = d_i*2^-i, one
+// rounding each (the product c_i*y is exact for normal values).  Only x of
+// the last iteration is used.  Returns x_n (before the 1/K(n) compensation).
+//
+// Instruction economy, bit-identical for normal sa:
+//  - iteration 0 (scale 1, y = 0) maps (sa, 0) to (sa, sa): a copy;
+//  - iteration 1 (d_1 = -1) gives x = fl(1.5 sa) and y = sa/2 exactly, so y
+//    is carried from here on as ys = 2y (scaling by 2 commutes with
+//    rounding): ys = sa costs nothing, and later iterations use
+//    x' = x - (c_i/2)*ys, ys' = ys + (2 c_i)*x, still one rounding each.
+// That is 2n - 3 FFMAs for n micro-rotations (plus the LOP3 fold, the 1/K(n)
+// FMUL and the accumulating FFMA: 2n - 1 instructions per MAC).
 template <int ITERS>
 __device__ __forceinline__ float gemm_cordic_x(float sa) {
-    float x = sa, y = sa;
+    static_assert(gemm_dir(1) < 0, "the y = sa/2 shortcut needs d_1 = -1");
+    if constexpr (ITERS <= 1) {
+        return sa;
+    } else {
+        float x = __fmaf_rn(-gemm_coef(1), sa, sa);       // iteration 1
+        float ys = sa;                                     // 2 * y_2
 #pragma unroll
-    for (int t = 1; t < ITERS; ++t) {
-        const float c = gemm_coef(t);
-        if (t == ITERS - 1) {
-            x = __fmaf_rn(-c, y, x);
-        } else {
-            const float xn = __fmaf_rn(-c, y, x);
-            y = __fmaf_rn(c, x, y);
-            x = xn;
+        for (int t = 2; t < ITERS; ++t) {
+            const float c = gemm_coef(t);
+            if (t == ITERS - 1) {
+                x = __fmaf_rn(-0.5f * c, ys, x);
+            } else {
+                const float xn = __fmaf_rn(-0.5f * c, ys, x);
+                ys = __fmaf_rn(2.0f * c, x, ys);
+                x = xn;
+            }
         }
+        return x;
     }
-    return x;
 }
 
 // Runtime-iteration variant (any n in [1, 24]); coefficients come from a
