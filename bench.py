@@ -369,7 +369,7 @@ def _splits(M: int, N: int, K: int, sms: int) -> int:
     if M <= 32:
         tiles = -(-M // 16) * -(-N // 128)
     else:
-        cands = [(-(-M // bm) * -(-N // bn), bm * bn) for bm, bn in ((64, 128), (64, 64), (32, 64))]
+        cands = [(-(-M // bm) * -(-N // bn), bm * bn) for bm, bn in ((64, 64), (32, 64))]
         tiles = min(cands, key=lambda c: (-(-c[0] // sms)) * c[1])[0]
     if tiles >= sms or K < 1024:
         return 1

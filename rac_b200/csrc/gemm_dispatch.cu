@@ -151,18 +151,22 @@ void keep_device_pool() {
 
 static int sm_count();
 
-// 3 for M <= 32.  Otherwise the tile (64x128, 64x64 or 32x64) that minimises
-// the work of the most loaded SM, ceil(tiles / SMs) x tile area -- the GEMM is
+// 3 for M <= 32.  Otherwise the 64x64 or 32x64 tile that minimises the work
+// of the most loaded SM, ceil(tiles / SMs) x tile area -- the GEMM is
 // issue-bound per SM, so that is its run time; ties go to the larger tile.
-// Variants 1-4 can be forced.
+// The 64x128 tile (8x8 per thread) is not chosen automatically: its unrolled
+// k-step is twice as long, and at n = 16 / 24 it measured 2 % / 28 % slower
+// than 64x64 (instruction-cache pressure).  Kernels without the 64x64 and
+// 32x64 instances (FAST, SHIFTADD, run-time n) use 64x128.  Variants 1-4 can
+// be forced.
 static int tile_variant(const GemmParams& p, int variant) {
     if (variant >= 1 && variant <= 4) return variant;
     if (p.M <= 32) return 3;
     const long long sms = sm_count();
-    const int bms[3] = {64, 64, 32}, bns[3] = {128, 64, 64}, vs[3] = {1, 2, 4};
-    int best = 1;
+    const int bms[2] = {64, 32}, bns[2] = {64, 64}, vs[2] = {2, 4};
+    int best = 2;
     long long best_cost = -1;
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 2; ++i) {
         const long long tiles = (long long)((p.M + bms[i] - 1) / bms[i]) * ((p.N + bns[i] - 1) / bns[i]);
         const long long cost = (tiles + sms - 1) / sms * bms[i] * bns[i];
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = vs[i]; }
