@@ -301,24 +301,90 @@ RAC_API int rac_check_device_errors(void* stream) {
 
 // ── blocking entry points (rac.h and batch forms) ───────────────────────
 
+// rac_matmul with host-resident A and C: the transfers are pipelined with
+// the compute.  B goes first; A follows in two row blocks on a copy stream,
+// and each block's GEMM starts on the compute stream as soon as its rows have
+// landed, while the previous block's C rows travel back.  Two blocks keep
+// each launch large enough to fill the SMs (the GEMM's per-SM balance is
+// unchanged: 4096 rows -> 2 x 2048).  Each output element's arithmetic does
+// not depend on the row blocking, so the result equals one launch's, except
+// where a block's shape selects split-K (few output tiles, K >= 1024), whose
+// partial sums associate differently.
+static int matmul_pipelined(Call& c, const float* A, const float* dB, float* C, int M, int N, int K,
+                            int iters, int mode) {
+    thread_local std::vector<cudaStream_t> copy_streams;
+    if ((int)copy_streams.size() <= c.dev) copy_streams.resize(c.dev + 1, nullptr);
+    if (!copy_streams[c.dev] && cudaStreamCreateWithFlags(&copy_streams[c.dev], cudaStreamNonBlocking) != cudaSuccess)
+        return kErrCuda;
+    cudaStream_t cs = copy_streams[c.dev];
+    float* dA = nullptr;
+    float* dC = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&dA), sizeof(float) * (size_t)M * K, c.s) != cudaSuccess ||
+        cudaMallocAsync(reinterpret_cast<void**>(&dC), sizeof(float) * (size_t)M * N, c.s) != cudaSuccess) {
+        cudaGetLastError();
+        if (dA) cudaFreeAsync(dA, c.s);
+        return kErrAlloc;
+    }
+    constexpr int kBlocks = 2;
+    cudaEvent_t ev[2 * kBlocks + 1];
+    for (auto& e : ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    // the copy stream may only write dA / dC after the allocations exist
+    cudaEventRecord(ev[2 * kBlocks], c.s);
+    cudaStreamWaitEvent(cs, ev[2 * kBlocks], 0);
+    int st = kOk;
+    GemmParams p{};
+    p.B = dB; p.N = N; p.K = K; p.lda = K; p.ldb = N; p.ldc = N; p.ldcin = N;
+    p.alpha = 1.0f; p.beta = 0.0f;
+    p.iters = iters;
+    for (int r = 0; r < kBlocks && st == kOk; ++r) {
+        const int m0 = (int)((long long)M * r / kBlocks), m1 = (int)((long long)M * (r + 1) / kBlocks);
+        if (m1 <= m0) continue;
+        const size_t a_off = (size_t)m0 * K, c_off = (size_t)m0 * N;
+        if (cudaMemcpyAsync(dA + a_off, A + a_off, sizeof(float) * (size_t)(m1 - m0) * K,
+                            cudaMemcpyHostToDevice, cs) != cudaSuccess) { st = kErrCuda; break; }
+        cudaEventRecord(ev[2 * r], cs);
+        cudaStreamWaitEvent(c.s, ev[2 * r], 0);
+        p.A = dA + a_off; p.C = dC + c_off; p.Cin = p.C; p.M = m1 - m0;
+        st = launch_gemm(p, kNN, mode, 0, c.s);
+        cudaEventRecord(ev[2 * r + 1], c.s);
+        cudaStreamWaitEvent(cs, ev[2 * r + 1], 0);
+        if (st == kOk && cudaMemcpyAsync(C + c_off, dC + c_off, sizeof(float) * (size_t)(m1 - m0) * N,
+                                         cudaMemcpyDeviceToHost, cs) != cudaSuccess) st = kErrCuda;
+    }
+    if (cudaStreamSynchronize(cs) != cudaSuccess && st == kOk) st = kErrCuda;
+    // the frees are ordered after the copy stream's last use of dA / dC
+    cudaFreeAsync(dA, c.s);
+    cudaFreeAsync(dC, c.s);
+    for (auto& e : ev) cudaEventDestroy(e);
+    return st;
+}
+
 static int do_matmul(const float* A, const float* B, float* C, int M, int N, int K, int iters,
                      int mode) {
     if (!A || !B || !C) return kErrNullPtr;
     if (M <= 0 || N <= 0 || K <= 0) return kErrInvalidDim;
     Call c;
     if (c.begin() != kOk) return c.st;
+    init_knobs();
+    iters = clamp_gemm_iters(iters <= 0 ? g_iters.load() : iters);
+    mode = mode < 0 ? g_mode.load() : mode;
+    const bool host_a = !is_device_ptr(A), host_c = !is_device_ptr(C);
+    if (host_a && host_c && M >= 256) {
+        const float* dB = (const float*)c.map(B, sizeof(float) * (size_t)K * N, true, false);
+        const int st = c.st == kOk ? matmul_pipelined(c, A, dB, C, M, N, K, iters, mode) : c.st;
+        return c.finish(st, false);
+    }
     const float* dA = (const float*)c.map(A, sizeof(float) * (size_t)M * K, true, false);
     const float* dB = (const float*)c.map(B, sizeof(float) * (size_t)K * N, true, false);
     float* dC = (float*)c.map(C, sizeof(float) * (size_t)M * N, false, true);
     int st = kOk;
     if (c.st == kOk) {
-        init_knobs();
         GemmParams p{};
         p.A = dA; p.B = dB; p.C = dC; p.Cin = dC;
         p.M = M; p.N = N; p.K = K; p.lda = K; p.ldb = N; p.ldc = N; p.ldcin = N;
         p.alpha = 1.0f; p.beta = 0.0f;
-        p.iters = clamp_gemm_iters(iters <= 0 ? g_iters.load() : iters);
-        st = launch_gemm(p, kNN, mode < 0 ? g_mode.load() : mode, 0, c.s);
+        p.iters = iters;
+        st = launch_gemm(p, kNN, mode, 0, c.s);
     }
     return c.finish(st, false);
 }

@@ -242,3 +242,20 @@ def test_tma_staging_splitk_and_strided(cuda, orc):
     assert np.array_equal(got, ref)
     assert _normwise(got, orc.gemm(A, B, "nn", 1, 8)) <= NORM_TOL
     ext.check_device_errors()
+
+
+def test_rac_matmul_host_pipeline(cuda, orc):
+    """rac_matmul with host A and C runs the two-block copy/compute pipeline;
+    the result equals the restatement bit for bit (no split-K at this shape),
+    with B on the host or on the device."""
+    L = _lib.lib()
+    M, N, K = 1000, 512, 300
+    A, B = _operands(M, N, K, "nn", 99)
+    want = orc.gemm(A, B, "nn", 1, 16)
+    for dev_b in (False, True):
+        C = np.zeros((M, N), np.float32)
+        Bp = _t(B, cuda) if dev_b else B
+        bptr = Bp.data_ptr() if dev_b else _p(B)
+        L.rac_matmul_ex(_p(A), bptr, _p(C), M, N, K, 16, 1)
+        _lib.check()
+        assert np.array_equal(C, want), dev_b
