@@ -373,7 +373,12 @@ def _splits(M: int, N: int, K: int, sms: int) -> int:
         tiles = min(cands, key=lambda c: (-(-c[0] // sms)) * c[1])[0]
     if tiles >= sms or K < 1024:
         return 1
-    return max(1, min(-(-4 * sms // tiles), K // 256))
+    best, S = 1.0, 1
+    for c in range(2, K // 256 + 1):
+        share = -(-tiles * c // sms) / c
+        if share < best - 1e-9:
+            best, S = share, c
+    return S
 
 
 def run_stream(args, world, rank, local) -> dict | None:

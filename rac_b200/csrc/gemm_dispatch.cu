@@ -175,8 +175,9 @@ static int tile_variant(const GemmParams& p, int variant) {
 }
 
 // Split-K when the output tiles cannot fill the machine: fewer tiles than
-// SMs and K long enough that each chunk keeps >= 256 k-steps.  Target about
-// 4 resident CTAs per SM.  variant 10+S forces S splits (tests, sweeps).
+// SMs and K >= 1024.  S is chosen to minimise the most loaded SM's share of
+// the work, ceil(tiles * S / SMs) / S, over 2 <= S <= K / 256 (chunks keep at
+// least 256 k-steps); ties go to the smaller S.  variant 10+S forces S splits.
 int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
     (void)layout; (void)mode;
     const int v = tile_variant(p, variant);
@@ -187,9 +188,12 @@ int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
     if (variant >= 10) {
         S = variant - 10;
     } else if (variant == 0 && tiles < sm_count() && p.K >= 1024) {
-        const long long target = 4LL * sm_count();
-        S = (int)((target + tiles - 1) / tiles);
-        if (S > p.K / 256) S = p.K / 256;
+        const long long sms = sm_count();
+        double best = 1.0;                                   // S = 1: the whole tile on one SM
+        for (int c = 2; c <= p.K / 256; ++c) {
+            const double share = (double)((tiles * c + sms - 1) / sms) / c;
+            if (share < best - 1e-9) { best = share; S = c; }
+        }
     }
     if (S < 1) S = 1;
     if (S > p.K) S = p.K;
