@@ -339,6 +339,19 @@ def run_matmul(args, world, rank, local) -> dict | None:
     te = max_over_ranks(statistics.mean(ts), world)
     assert torch.equal(Ch, C.cpu()), "e2e result differs from the device-resident run"
 
+    # Context: cuBLAS SGEMM (torch.matmul, fp32, TF32 off) on the same operands.
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for _ in range(3):
+        torch.matmul(A, B)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        torch.matmul(A, B)
+    e1.record()
+    torch.cuda.synchronize()
+    t_cublas = e0.elapsed_time(e1) / reps
     if rank != 0:
         return None
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -358,6 +371,10 @@ def run_matmul(args, world, rank, local) -> dict | None:
         "e2e": {"value": 2.0 * M * N * K / te / 1e9, "unit": "GOP/s",
                 "h2d_bytes_per_step": 4 * (M * K + K * Nl), "d2h_bytes_per_step": 4 * M * Nl,
                 "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"},
+        "context": {"cublas_sgemm": {"value": 2.0 * M * Nl * K / (t_cublas * 1e-3) / 1e9,
+                                     "unit": "GFLOP/s", "ms": t_cublas,
+                                     "note": "torch.matmul fp32 (TF32 off) on this rank's operands; "
+                                             "plain FMA SGEMM, not the CORDIC arithmetic"}},
         "gpu_launches": args.steps * (2 if _splits(M, N // world, K, sms) > 1 else 1),
         "clocks": clk.summary(),
     }
