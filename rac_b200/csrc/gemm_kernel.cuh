@@ -147,6 +147,12 @@ k_gemm(const __grid_constant__ GemmParams p) {
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
+    // Ownership: a thread's TM rows (TN columns) are TM/4 (TN/4) groups of 4
+    // consecutive rows (columns) spaced BM/(TM/4) (BN/(TN/4)) apart, so the
+    // float4 shared-memory reads of a warp are contiguous (bank-conflict
+    // free).  Which thread owns an output does not change its arithmetic.
+    auto row_of = [&](int i) { return (i >> 2) * (BM / (TM / 4)) + ty * 4 + (i & 3); };
+    auto col_of = [&](int j) { return (j >> 2) * (BN / (TN / 4)) + tx * 4 + (j & 3); };
     // K range of this CTA: all of K, or one split-K chunk (kchunk % BK == 0).
     const int kbeg = p.ws ? blockIdx.z * p.kchunk : 0;
     const int kend = p.ws ? min(p.K, kbeg + p.kchunk) : p.K;
@@ -167,22 +173,22 @@ k_gemm(const __grid_constant__ GemmParams p) {
         if constexpr (A_KMAJOR) {
 #pragma unroll
             for (int i = 0; i < TM; i += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(&Asb[kk * BM + ty * TM + i]);
+                const float4 v = *reinterpret_cast<const float4*>(&Asb[kk * BM + row_of(i)]);
                 a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < TM; ++i) a[i] = Asb[(ty * TM + i) * BK + kk];
+            for (int i = 0; i < TM; ++i) a[i] = Asb[row_of(i) * BK + kk];
         }
         if constexpr (B_KMAJOR) {
 #pragma unroll
             for (int j = 0; j < TN; j += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(&Bsb[kk * BN + tx * TN + j]);
+                const float4 v = *reinterpret_cast<const float4*>(&Bsb[kk * BN + col_of(j)]);
                 b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < TN; ++j) b[j] = Bsb[(tx * TN + j) * BK + kk];
+            for (int j = 0; j < TN; ++j) b[j] = Bsb[col_of(j) * BK + kk];
         }
         if constexpr (MODE == kFast) {
 #pragma unroll
@@ -283,11 +289,11 @@ k_gemm(const __grid_constant__ GemmParams p) {
         float* w = p.ws + (long long)blockIdx.z * p.M * p.N;
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
-            const int gm = m0 + ty * TM + i;
+            const int gm = m0 + row_of(i);
             if (gm >= p.M) continue;
 #pragma unroll
             for (int j = 0; j < TN; ++j) {
-                const int gn = n0 + tx * TN + j;
+                const int gn = n0 + col_of(j);
                 if (gn < p.N) w[(long long)gm * p.N + gn] = acc[i][j];
             }
         }
@@ -297,11 +303,11 @@ k_gemm(const __grid_constant__ GemmParams p) {
     // for bias + activation).
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
-        const int gm = m0 + ty * TM + i;
+        const int gm = m0 + row_of(i);
         if (gm >= p.M) continue;
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
-            const int gn = n0 + tx * TN + j;
+            const int gn = n0 + col_of(j);
             if (gn >= p.N) continue;
             float v;
             if (p.beta != 0.0f)
