@@ -144,16 +144,25 @@ __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
 // direction d_i = (angle_i >= 0) ? +1 : -1 is the sign of the residual angle.
 // (x, y) arrive pre-scaled.  Returns false when the wrap loop hit kWrapLimit.
 //
-// Instruction economy (5 per micro-rotation, bit-identical):
-//  - iteration 0 takes the comparison itself (the folded input angle may be
-//    -0, which counts as >= 0);
-//  - for i >= 1, d_i = +-1.0 is built from the angle's sign bit with one
-//    LOP3 ((bits & sign) | bits(1.0), both masks in registers): a later
-//    angle is never -0 (an exact-zero difference rounds to +0);
-//  - d_i * 2^-i is one FMUL (exact), and angle - d_i * atan_i one FFMA with a
-//    single rounding, as the reference's subtraction of the exact product;
-//  - a NaN angle (NaN input) takes its own loop, d = -1 throughout, as every
-//    comparison with NaN is false in the reference.
+// Pipe balance: the direction of iterations i >= 1 is computed on the FMA
+// pipe, not with sign-bit logic on the (half-rate) ALU pipe:
+//   t_i = sat(angle_i * 2^126 + 1)          -> 1 if angle_i >= 0 (incl. -0),
+//                                              0 if angle_i < 0 or NaN
+//   d_i = 2 t_i - 1,  d_i * 2^-i and d_i * atan_i exact (d_i = +-1)
+// This equals the comparison whenever angle_i is 0 or |angle_i| >= 2^-125.
+// For i >= 1 that always holds: angle_1 = fl(angle_0 -+ atan_0) has
+// magnitude >= 2^-2 or is a difference of floats near atan_0 (a multiple of
+// 2^-25), and every later angle is a rounded sum of it and table entries,
+// hence 0 or a multiple of 2^-48.  Iteration 0 (arbitrary input angle,
+// possibly subnormal) uses the comparison itself.
+// sat(a * b + c) as one FFMA.SAT (PTX fma.rn.sat.f32: result clamped to
+// [0, 1], NaN -> +0).
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+    float r;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 template <int ITERS>
 __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta) {
     const float TAU = 2.0f * kPi;
@@ -167,37 +176,28 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta)
     } else if (theta < -kPi * 0.5f) {
         x = -x; y = -y; theta = __fadd_rn(theta, kPi);
     }
-    if (theta != theta) {
-        float s = 1.0f;
-#pragma unroll
-        for (int i = 0; i < ITERS; ++i) {
-            const float xn = __fmaf_rn(s, y, x);
-            y = __fmaf_rn(-s, x, y);
-            x = xn;
-            s *= 0.5f;
-        }
-        xr = x; yr = y;
-        return ok;
-    }
     float angle = theta;
     {   // iteration 0: scale 1
         const float d = (angle >= 0.0f) ? 1.0f : -1.0f;
         const float xn = __fmaf_rn(-d, y, x);
         y = __fmaf_rn(d, x, y);
         x = xn;
-        if (ITERS > 1) angle = __fmaf_rn(-d, atan_entry(0), angle);
+        if (ITERS > 1) angle = __fsub_rn(angle, d * atan_entry(0));
     }
-    uint32_t sign_mask = 0x80000000u, one_bits = 0x3f800000u;
-    asm volatile("" : "+r"(sign_mask), "+r"(one_bits));   // keep both in registers
+    // Each instruction below carries at most one immediate (FFMA encodes one);
+    // the +1 / -1 addends live in registers, so an iteration is exactly six
+    // FMA-pipe instructions with no constant materialisation.
+    const float one = 1.0f, neg_one = -1.0f;
 #pragma unroll
     for (int i = 1; i < ITERS; ++i) {
-        const float d = __uint_as_float((__float_as_uint(angle) & sign_mask) | one_bits);
-        const float ds = __fmul_rn(d, pow2neg(i));          // d_i * 2^-i (exact)
+        const float t = fma_sat(angle, 0x1p126f, one);     // 1: angle >= 0, 0: < 0 / NaN
+        const float e = __fmaf_rn(t, 2.0f, neg_one);       // d_i = +-1
+        const float ds = __fmul_rn(e, pow2neg(i));          // d_i * 2^-i (exact)
         const float xn = __fmaf_rn(-ds, y, x);
         y = __fmaf_rn(ds, x, y);
         x = xn;
         if (i + 1 < ITERS)
-            angle = __fmaf_rn(-d, atan_entry(i), angle);     // angle - d_i*atan_i, one rounding
+            angle = __fmaf_rn(-e, atan_entry(i), angle);    // angle - d_i*atan_i, one rounding
     }
     xr = x; yr = y;
     return ok;
