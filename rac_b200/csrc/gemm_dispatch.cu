@@ -260,7 +260,6 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
 int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
     GemmParams p = p_in;
     const bool tma = use_tma(variant);
-    const int variant_flags = variant;
     variant &= 0xff;
     int v = tile_variant(p, variant);
     int dev = 0;
@@ -272,15 +271,7 @@ int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, 
     const int b_contig = (layout == kNT) ? p.K : p.N;
     const bool vec = aligned16(p.A) && aligned16(p.B) && (p.lda % 4 == 0) &&
                      (p.ldb % 4 == 0) && (a_contig % 4 == 0) && (b_contig % 4 == 0);
-    if (mode == kFast) {
-        // Paired-FMA kernel for aligned whole-K problems (variant bit 0x400 or
-        // a forced tile selects the general kernel instead).
-        if (vec && !p.ws && !(variant_flags & 0x400) && variant == 0 && p.M > 32) {
-            const int st = launch_gemm_fast(p, layout, s);
-            if (st != kErrUnsupported) return st;
-        }
-        return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
-    }
+    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
     if (mode == kShiftAdd) {
         if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
         return pick_layout<kShiftAdd, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);

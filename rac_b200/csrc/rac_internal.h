@@ -59,9 +59,6 @@ bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK);
 // as given (p.ws == nullptr: whole K per CTA).
 int launch_gemm_into(const GemmParams& p, int layout, int mode, int variant,
                      cudaStream_t stream);
-// FAST-mode GEMM on the paired-FMA kernel (gemm_fast.cu); kErrUnsupported
-// when the operands do not fit it (split-K, unaligned).
-int launch_gemm_fast(const GemmParams& p, int layout, cudaStream_t stream);
 // Sums ws[0..splits-1][M][N] in order and applies the GEMM epilogue of p.
 int launch_splitk_reduce(const GemmParams& p, cudaStream_t stream);
 // Number of K splits launch_gemm uses for this problem (1 = none).
