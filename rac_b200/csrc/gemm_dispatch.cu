@@ -260,11 +260,17 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
 int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, cudaStream_t s) {
     GemmParams p = p_in;
     const bool tma = use_tma(variant);
+    const int hooks = variant;
     variant &= 0xff;
     int v = tile_variant(p, variant);
     int dev = 0;
     cudaGetDevice(&dev);
     p.err = device_error_word(dev);
+    // Variant bit 0x1000 is a test hook: each stage barrier expects 16 bytes
+    // more than its copies deliver and gives up after 4096 polls, so the
+    // bounded-wait path (error word bit 1, no hang) can be exercised.
+    p.tma_wait_limit = (hooks & 0x1000) ? 4096u : kTmaWaitLimit;
+    p.tma_extra_tx = (hooks & 0x1000) ? 16u : 0u;
     // Vector loads need 16-byte aligned bases, leading dims that are
     // multiples of 4 and contiguous extents that are multiples of 4.
     const int a_contig = (layout == kTN) ? p.M : p.K;

@@ -122,8 +122,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
                  :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
                     "r"(smem_u32(bar)) : "memory");
 }
-// Upper bound on the polls of one stage barrier: a copy that never lands sets
-// bit 1 of the device error word instead of hanging the kernel.
+// Default upper bound on the polls of one stage barrier: a copy that never
+// lands sets bit 1 of the device error word instead of hanging the kernel.
 constexpr uint32_t kTmaWaitLimit = 1u << 22;
 
 template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC,
@@ -229,7 +229,7 @@ k_gemm(const __grid_constant__ GemmParams p) {
         constexpr uint32_t kStageBytes = sizeof(float) * (BM + BN) * BK;
         auto issue = [&](int stage, int k0) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_expect_tx(&full_bar[stage], kStageBytes);
+            mbar_expect_tx(&full_bar[stage], kStageBytes + p.tma_extra_tx);
             if constexpr (A_KCOLS) tma_load_2d(As[stage], &p.tmA, k0, m0, &full_bar[stage]);
             else                   tma_load_2d(As[stage], &p.tmA, m0, k0, &full_bar[stage]);
             if constexpr (B_KCOLS) tma_load_2d(Bs[stage], &p.tmB, k0, n0, &full_bar[stage]);
@@ -250,13 +250,15 @@ k_gemm(const __grid_constant__ GemmParams p) {
             if (!timed_out) {
                 uint32_t polls = 0;
                 while (!mbar_try_wait(&full_bar[st], parity)) {
-                    if (++polls >= kTmaWaitLimit) { timed_out = true; break; }
+                    if (++polls >= p.tma_wait_limit) { timed_out = true; break; }
                 }
             }
 #pragma unroll 1
             for (int kk = 0; kk < BK; ++kk) mac_step(As[st], Bs[st], kk);
             __syncthreads();                       // every thread is done with stage st
-            if (tid == 0 && kt + STAGES < ktiles) issue(st, kbeg + (kt + STAGES) * BK);
+            // After a timeout the stage's phase never completed; re-arming it
+            // would arrive on a barrier with no pending arrivals, so stop.
+            if (tid == 0 && !timed_out && kt + STAGES < ktiles) issue(st, kbeg + (kt + STAGES) * BK);
         }
         if (timed_out && p.err) atomicOr(p.err, 2u);
     } else {

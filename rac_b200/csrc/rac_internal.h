@@ -48,6 +48,8 @@ struct GemmParams {
     alignas(64) CUtensorMap tmA;
     alignas(64) CUtensorMap tmB;
     unsigned int* err;
+    unsigned int tma_wait_limit;   // polls of a stage barrier before giving up
+    unsigned int tma_extra_tx;     // test hook: bytes expected beyond the copies (0)
 };
 
 // Fills p.tmA / p.tmB for a TMA-staged launch with a BM x BN x BK tile.

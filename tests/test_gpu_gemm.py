@@ -259,3 +259,19 @@ def test_rac_matmul_host_pipeline(cuda, orc):
         L.rac_matmul_ex(_p(A), bptr, _p(C), M, N, K, 16, 1)
         _lib.check()
         assert np.array_equal(C, want), dev_b
+
+
+def test_tma_wait_limit_reports_error_and_context_survives(cuda, orc):
+    """Failure detection without a fault: with the test hook (variant 0x1000)
+    every stage barrier expects 16 bytes more than its copies deliver, so the
+    bounded wait runs out; the kernel flags the device error word, the host
+    reads RAC_ERR_DEVICE, and the next GEMM on the same context is exact."""
+    A, B = _operands(128, 128, 64, "nn", 1)
+    dA, dB = _t(A, cuda), _t(B, cuda)
+    ext.gemm(dA, dB, LAYOUT_NN, 16, 1, variant=TMA | 0x1000)
+    with pytest.raises(_lib.RacError) as e:
+        ext.check_device_errors()
+    assert e.value.status == -6
+    got = ext.gemm(dA, dB, LAYOUT_NN, 16, 1, variant=TMA).cpu().numpy()
+    assert np.array_equal(got, orc.gemm(A, B, "nn", 1, 16))
+    ext.check_device_errors()
