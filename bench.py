@@ -405,6 +405,7 @@ def run_stream(args, world, rank, local) -> dict | None:
     dev = torch.device("cuda", local)
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     w = args.workload
+    launches_per_step = 2 if w == "rope" else 1
     if w == "rotate":
         n = 1 << args.log2n
         v = torch.randn((n, 2), device=dev, generator=g)
@@ -415,10 +416,14 @@ def run_stream(args, world, rank, local) -> dict | None:
         cfg = f"rac_rotate_batch_n 2^{args.log2n} float2 ~N(0,1), theta U[-pi,pi), {args.iters} iterations"
     elif w == "rope":
         q = torch.randn((8, 32, 4096, 128), device=dev, generator=g)
+        kk = torch.randn((8, 32, 4096, 128), device=dev, generator=g)
         ctab, stab = ext.rope_cache(4096, 128, 10000.0, device=dev)
-        fn = lambda: ext.rope_apply_(q, ctab, stab)               # noqa: E731
-        bytes_, units, unit_name = 8 * q.numel(), q.numel(), "Gelem/s"
-        cfg = "rac_rope_apply Q [8,32,4096,128] fp32 in place, base 1e4"
+
+        def fn():
+            ext.rope_apply_(q, ctab, stab)
+            ext.rope_apply_(kk, ctab, stab)
+        bytes_, units, unit_name = 2 * 8 * q.numel(), 2 * q.numel(), "Gelem/s"
+        cfg = "rac_rope_apply Q and K [8,32,4096,128] fp32 in place, base 1e4"
     elif w == "attention":
         qa, ka, va = [torch.randn((4, 32, 2048, 128), device=dev, generator=g) for _ in range(3)]
         ao = torch.empty_like(qa)
@@ -492,7 +497,7 @@ def run_stream(args, world, rank, local) -> dict | None:
                      "frac": ach / peak, "peak_basis": "of measured" if "hbm_gbs" in peaks else "of fallback",
                      "frac_of_8TBs": ach / 8000.0, "kernel_ms": t_local,
                      "traffic": load_traffic().get(f"{w}")},
-        "gpu_launches": args.steps, "clocks": clk.summary(),
+        "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
     }
 
 

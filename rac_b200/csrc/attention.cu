@@ -21,6 +21,7 @@
 // HD/8 columns in float4 groups.  Shared rows are padded by 4 floats so that
 // the float4 reads of K, V and P are bank-conflict free.
 #include <cmath>
+#include <mutex>
 
 #include "rac_internal.h"
 #include "stream_ops.h"
@@ -205,14 +206,15 @@ template <int HD>
 static int launch_att(const float* q, const float* k, const float* v, const float* mask, int causal,
                       float* out, int batch, int heads, int seq, float scale, cudaStream_t s) {
     const size_t smem = AttSmem<HD>::bytes;
-    static bool attr_set[64] = {};
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kErrCuda;
-        attr_set[dev] = true;
-    }
+    if (dev < 0 || dev >= 64) return kErrUnsupported;
+    std::call_once(once[dev], [dev, smem] {
+        attr_err[dev] = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    if (attr_err[dev] != cudaSuccess) return kErrCuda;
     const dim3 grid((seq + kAttBQ - 1) / kAttBQ, heads, batch);
     if (grid.y > 65535 || grid.z > 65535) return kErrInvalidDim;
     k_attention<HD><<<grid, kAttThreads, smem, s>>>(q, k, v, mask, causal, out, heads, seq, scale);

@@ -1,4 +1,5 @@
 // gemm_dispatch.cu -- picks the GEMM kernel instance for a call.
+#include <atomic>
 #include <cstdlib>
 #include <cudaTypedefs.h>
 #include <mutex>
@@ -84,12 +85,11 @@ bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK) {
 static bool use_tma(int variant) {
     if (variant & 0x100) return true;
     if (variant & 0x200) return false;
-    static int env = -1;
-    if (env < 0) {
+    static const bool env = [] {
         const char* e = std::getenv("RAC_GEMM_TMA");
-        env = (e && e[0] == '0') ? 0 : 1;
-    }
-    return env == 1;
+        return !(e && e[0] == '0');
+    }();
+    return env;
 }
 
 template <int MODE, int ITERS, int LAYOUT>
@@ -123,16 +123,17 @@ static int pick_fixed(const GemmParams& p, int layout, int v, cudaStream_t s) {
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 static int sm_count() {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (!n) {
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cached[dev] = n > 0 ? n : 148;
+        if (n <= 0) n = 148;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 void keep_device_pool() {

@@ -5,6 +5,8 @@
 // and a grid-stride loop over a grid sized to the SM count.  The arithmetic
 // follows lib/c/rac_cpu.c rounding step by rounding step (see
 // rac_device.cuh), so results are bit-identical to the reference library.
+#include <atomic>
+
 #include "rac_device.cuh"
 #include "rac_internal.h"
 #include "stream_ops.h"
@@ -14,14 +16,17 @@ namespace racb {
 __device__ unsigned int g_err_word;   // per device: bit 0 = wrap-loop overrun
 
 unsigned int* device_error_word(int device) {
-    static unsigned int* cache[64] = {};
+    // Looked up once per device (that device current), then read lock-free.
+    static std::atomic<unsigned int*> cache[64] = {};
     if (device < 0 || device >= 64) return nullptr;
-    if (!cache[device]) {
+    unsigned int* w = cache[device].load(std::memory_order_acquire);
+    if (!w) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) return nullptr;
-        cache[device] = static_cast<unsigned int*>(p);
+        if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        w = static_cast<unsigned int*>(p);
+        cache[device].store(w, std::memory_order_release);
     }
-    return cache[device];
+    return w;
 }
 
 static int grid_for(long long work_items, int threads) {
