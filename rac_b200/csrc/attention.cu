@@ -34,32 +34,8 @@ template <int HD>
 struct AttSmem {
     static constexpr int LD = HD + 4;             // padded row (floats)
     static constexpr int PLD = kAttBK + 4;
-    // Q, K, V tiles and the P tile.
-    static constexpr size_t bytes = sizeof(float) * (3 * kAttBQ * LD + kAttBQ * PLD);
+    static constexpr size_t bytes = sizeof(float) * (2 * kAttBQ * LD + kAttBQ * PLD);
 };
-
-// 16-byte asynchronous global->shared copy (cp.async.cg); src_bytes = 0
-// zero-fills the destination (rows past the end of the sequence).
-__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
-    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
-                 :: "r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-template <int HD>
-__device__ __forceinline__ void load_tile_async(float* dst, const float* __restrict__ src, int row0,
-                                                int rows_valid) {
-    constexpr int LD = AttSmem<HD>::LD;
-    constexpr int QPR = HD / 4;
-    for (int e = threadIdx.x; e < kAttBQ * QPR; e += kAttThreads) {
-        const int r = e / QPR, c = (e % QPR) * 4;
-        const bool ok = row0 + r < rows_valid;
-        cp_async16(dst + r * LD + c, src + (long long)(ok ? row0 + r : 0) * HD + c, ok);
-    }
-    cp_async_commit();
-}
 
 template <int HD>
 __device__ __forceinline__ void load_tile(float* dst, const float* __restrict__ src, int row0,
@@ -121,16 +97,15 @@ __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, 
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kAttThreads, 1)
+__global__ void __launch_bounds__(kAttThreads, 2)
 k_attention(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
             const float* __restrict__ mask, int causal, float* __restrict__ out, int heads, int seq,
             float scale) {
     constexpr int LD = AttSmem<HD>::LD, PLD = AttSmem<HD>::PLD, CG = HD / 32;
     extern __shared__ __align__(16) float smem[];
     float* Qs = smem;
-    float* Ks = Qs + kAttBQ * LD;
-    float* Vs = Ks + kAttBQ * LD;
-    float* Ps = Vs + kAttBQ * LD;
+    float* KVs = Qs + kAttBQ * LD;
+    float* Ps = KVs + kAttBQ * LD;
 
     const int nqb = (seq + kAttBQ - 1) / kAttBQ;
     const int qb = nqb - 1 - blockIdx.x;          // heaviest (causal) blocks first
@@ -155,16 +130,13 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int g = 0; g < CG; ++g) o[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    // Copies overlap compute: V(kb) streams in while the scores and softmax
-    // of tile kb run; K(kb+1) streams in while P V of tile kb runs.
-    load_tile_async<HD>(Ks, kh, 0, seq);
     for (int kb = 0; kb < nkb; ++kb) {
-        cp_async_wait_all();
-        __syncthreads();                      // K(kb) landed; V, P free again
-        load_tile_async<HD>(Vs, vh, kb * kAttBK, seq);
+        __syncthreads();
+        load_tile<HD>(KVs, kh, kb * kAttBK, seq);
+        __syncthreads();
         float sc[4][8];
-        tile_scores<HD>(sc, Qs, Ks, t0, kb * kAttBK, seq, scale, causal, mask);
-        #pragma unroll
+        tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
+#pragma unroll
         for (int i = 0; i < 4; ++i) {
             float tm = sc[i][0];
 #pragma unroll
@@ -188,9 +160,9 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
                 Ps[(rg + 16 * i) * PLD + cg + 8 * j] = e;
             }
         }
-        cp_async_wait_all();
-        __syncthreads();                      // V(kb) landed, P visible, K free
-        if (kb + 1 < nkb) load_tile_async<HD>(Ks, kh, (kb + 1) * kAttBK, seq);
+        __syncthreads();
+        load_tile<HD>(KVs, vh, kb * kAttBK, seq);
+        __syncthreads();
         const int kmax = min(kAttBK, seq - kb * kAttBK);
         for (int s = 0; s < kmax; ++s) {
             float p[4];
@@ -198,7 +170,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
             for (int i = 0; i < 4; ++i) p[i] = Ps[(rg + 16 * i) * PLD + s];
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
-                const float4 vv = *reinterpret_cast<const float4*>(Vs + s * LD + cg * 4 + 32 * g);
+                const float4 vv = *reinterpret_cast<const float4*>(KVs + s * LD + cg * 4 + 32 * g);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     o[i][g].x = __fmaf_rn(p[i], vv.x, o[i][g].x);
