@@ -1,0 +1,159 @@
+"""Real-weight loading: safetensors reader/writer and the Llama-layer mapping.
+
+The reference decoder reads F32 / F16 / BF16 safetensors
+(bench/safetensors_reader.c) and loads `model.layers.L.*` by the HF Llama
+names (bench/bench_rac_transformer.c:182-190).  The mapping is pinned
+against transformers' own LlamaDecoderLayer (rotate-half RoPE, grouped-query
+K/V): the CPU tests check the loaded block's parameters in plain torch fp32,
+the GPU test runs the block on this library's kernels.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from rac_b200 import weights as W
+
+
+def _hf_layer(d=128, heads=4, kv=2, ff=192, seed=0):
+    tr = pytest.importorskip("transformers")
+    from transformers.models.llama.modeling_llama import LlamaDecoderLayer, LlamaRotaryEmbedding
+    cfg = tr.LlamaConfig(hidden_size=d, intermediate_size=ff, num_attention_heads=heads,
+                         num_key_value_heads=kv, rms_norm_eps=1e-5, max_position_embeddings=64,
+                         attn_implementation="eager")
+    torch.manual_seed(seed)
+    layer = LlamaDecoderLayer(cfg, 0).eval()
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.copy_(torch.randn_like(p) * (0.08 if p.dim() == 2 else 0.3) + (1.0 if p.dim() == 1 else 0.0))
+    return cfg, layer, LlamaRotaryEmbedding(cfg)
+
+
+def _hf_forward(layer, rot, x):
+    B, T, _ = x.shape
+    pos = torch.arange(T)[None].expand(B, T)
+    mask = torch.full((T, T), float("-inf")).triu(1)[None, None].expand(B, 1, T, T)
+    with torch.no_grad():
+        return layer(x, attention_mask=mask, position_embeddings=rot(x, pos), position_ids=pos)
+
+
+def _plain_block(blk, x):
+    """RACLlamaBlock's math in plain torch fp32 (interleaved RoPE, MHA)."""
+    a = blk.attn
+    H, hd = a.n_heads, a.d_head
+    B, T, d = x.shape
+
+    def rms(v, m):
+        return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + m.eps) * m.weight
+
+    q, k, v = (rms(x, blk.norm1) @ a.qkv.weight.T).chunk(3, -1)
+    q, k, v = (t.view(B, T, H, hd).transpose(1, 2) for t in (q, k, v))
+    c, s = a.rope.cos_cache[:T], a.rope.sin_cache[:T]
+
+    def rope(t):
+        t1, t2 = t[..., 0::2], t[..., 1::2]
+        return torch.stack([t1 * c - t2 * s, t1 * s + t2 * c], -1).flatten(-2)
+
+    o = F.scaled_dot_product_attention(rope(q), rope(k), v, is_causal=True)
+    h = x + o.transpose(1, 2).reshape(B, T, d) @ a.out_proj.weight.T
+    n = rms(h, blk.norm2)
+    f = blk.ffn
+    return h + (F.silu(n @ f.gate.weight.T) * (n @ f.up.weight.T)) @ f.down.weight.T
+
+
+def test_safetensors_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    t = {"a": rng.standard_normal((3, 5)).astype(np.float32),
+         "b.c": rng.standard_normal(7).astype(np.float32) * 1e3,
+         "empty": np.zeros((0, 4), np.float32)}
+    for dt in ("F32", "F16", "BF16"):
+        path = str(tmp_path / f"t_{dt}.safetensors")
+        W.write_safetensors(path, t, dtype=dt)
+        got = W.read_safetensors(path)
+        assert set(got) == set(t)
+        for k, v in t.items():
+            if dt == "F32":
+                want = v
+            elif dt == "F16":
+                want = v.astype(np.float16).astype(np.float32)
+            else:
+                want = torch.from_numpy(v).to(torch.bfloat16).float().numpy()
+            assert got[k].dtype == np.float32 and got[k].shape == v.shape
+            assert np.array_equal(got[k], want), (dt, k)
+    sub = W.read_safetensors(str(tmp_path / "t_F32.safetensors"), names={"a"})
+    assert list(sub) == ["a"]
+
+
+def test_safetensors_rejects_other_dtypes(tmp_path):
+    import json
+    import struct
+    path = tmp_path / "i.safetensors"
+    h = json.dumps({"__metadata__": {"format": "pt"},
+                    "x": {"dtype": "I32", "shape": [2], "data_offsets": [0, 8]}}).encode()
+    path.write_bytes(struct.pack("<Q", len(h)) + h + bytes(8))
+    with pytest.raises(ValueError, match="unsupported dtype I32"):
+        W.read_safetensors(str(path))
+
+
+def test_rotate_half_permutation():
+    w = torch.arange(2 * 8, dtype=torch.float32).reshape(8, 2)     # 1 head, hd 8
+    p = W.rotate_half_to_interleaved(w, 1)
+    # interleaved pair i = (rotate-half dims i, i + hd/2)
+    assert p[:, 0].tolist() == [0, 8, 2, 10, 4, 12, 6, 14]
+
+
+@pytest.mark.parametrize("dtype", ["F32", "BF16"])
+def test_llama_layer_mapping_matches_transformers(tmp_path, dtype):
+    cfg, layer, rot = _hf_layer()
+    sd = {f"model.layers.3.{k}": v.numpy() for k, v in layer.state_dict().items()}
+    path = str(tmp_path / "layer.safetensors")
+    W.write_safetensors(path, sd, dtype=dtype)
+    if dtype == "BF16":       # compare against the checkpoint as stored
+        with torch.no_grad():
+            for p in layer.parameters():
+                p.copy_(p.to(torch.bfloat16).float())
+    blk = W.load_llama_layer(path, 3, n_heads=4, rms_eps=1e-5, max_seq_len=64, device="cpu")
+    assert blk.gated and blk.attn.qkv.weight.shape == (3 * 128, 128)
+    x = torch.randn(2, 9, 128)
+    with torch.no_grad():
+        y = _plain_block(blk, x)
+    assert (y - _hf_forward(layer, rot, x)).abs().max() < 2e-5
+
+
+def test_llama_layer_errors(tmp_path):
+    cfg, layer, _ = _hf_layer()
+    sd = {f"model.layers.0.{k}": v.numpy() for k, v in layer.state_dict().items()}
+    with pytest.raises(KeyError, match="missing tensors"):
+        W.load_llama_layer(sd, 1, n_heads=4, device="cpu")
+    with pytest.raises(ValueError, match="multiple of n_kv_heads"):
+        W.load_llama_layer(sd, 0, n_heads=4, n_kv_heads=3, device="cpu")
+    bad = dict(sd)
+    bad["model.layers.0.mlp.down_proj.weight"] = np.zeros((128, 100), np.float32)
+    with pytest.raises(ValueError, match="down_proj.weight: shape"):
+        W.load_llama_layer(bad, 0, n_heads=4, device="cpu")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,tol", [("fast", 1e-4), ("cordic", 2e-3)])
+def test_llama_layer_on_gpu_matches_transformers(tmp_path, cuda, mode, tol):
+    from rac_b200 import rac_torch as R
+    cfg, layer, rot = _hf_layer()
+    sd = {f"model.layers.0.{k}": v.numpy() for k, v in layer.state_dict().items()}
+    path = str(tmp_path / "layer.safetensors")
+    W.write_safetensors(path, sd)
+    blk = W.load_llama_layer(path, 0, n_heads=4, n_kv_heads=2, rms_eps=1e-5, max_seq_len=64,
+                             device=cuda)
+    x = torch.randn(2, 33, 128)
+    want = _hf_forward(layer, rot, x)
+    R.rac_set_mode(mode)
+    R.rac_set_precision(24 if mode == "fast" else 16)
+    try:
+        with torch.no_grad():
+            y = blk(x.to(cuda), is_causal=True).cpu()        # fused attention + residual epilogues
+        y_g = blk(x.to(cuda), is_causal=True).detach().cpu()  # autograd path
+    finally:
+        R.rac_set_mode("fast")
+        R.rac_set_precision(24)
+    scale = want.abs().max().item()
+    assert (y - want).abs().max().item() < tol * scale
+    assert (y_g - want).abs().max().item() < tol * scale
