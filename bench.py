@@ -222,6 +222,34 @@ def cpu_stream_baseline(w: str, iters: int) -> dict | None:
     return {"value": units / t / 1e9, "unit": unit, "cores": cores, "kind": "reference", "sample": sample}
 
 
+def cpu_llama_baseline(size: int) -> dict:
+    """The reference RACLlamaBlock's CPU path (torch fp32 F.linear / matmul, which is
+    what the reference module runs off the GPU) on every host thread, on a bounded
+    sample: one sequence of 256 tokens through the full-width block."""
+    import torch
+    from oracle import torch_block as TB
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    d, H, ff = (4096, 32, 11008) if size == 4096 else (size, max(1, size // 128), int(size * 2.6875))
+    T = 256
+    g = torch.Generator().manual_seed(0)
+    w = lambda *shape: torch.randn(shape, generator=g) * 0.02          # noqa: E731
+    p = {"norm1": torch.ones(d), "qkv": w(3 * d, d), "out": w(d, d), "norm2": torch.ones(d),
+         "gate": w(ff, d), "up": w(ff, d), "down": w(d, ff)}
+    x = torch.randn((1, T, d), generator=g)
+    cos, sin = TB.rope_cache(d // H, T)
+    with torch.no_grad():
+        TB.block_forward(p, x, H, cos=cos, sin=sin)
+        reps = 3
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            TB.block_forward(p, x, H, cos=cos, sin=sin)
+        t = (time.perf_counter() - t0) / reps
+    return {"value": T / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"x [1,{T},{d}] through the gated block, torch fp32 on CPU "
+                      f"(the reference module's CPU path: F.linear/matmul, FMA not CORDIC)"}
+
+
 def run_reference(args) -> None:
     """--impl reference: the reference's own CPU rac_matmul on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -546,6 +574,8 @@ def main() -> None:
             else:
                 M = N = K = args.size
             out["cpu_baseline"] = cpu_matmul_baseline(M, N, K, args.iters)
+        if world == 1 and not args.no_cpu_baseline and args.workload == "llama":
+            out["cpu_baseline"] = cpu_llama_baseline(args.size)
         print(json.dumps(out))
     if world > 1:
         import torch.distributed as dist

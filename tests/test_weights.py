@@ -10,7 +10,6 @@ the GPU test runs the block on this library's kernels.
 import numpy as np
 import pytest
 import torch
-import torch.nn.functional as F
 
 from rac_b200 import weights as W
 
@@ -38,27 +37,10 @@ def _hf_forward(layer, rot, x):
 
 
 def _plain_block(blk, x):
-    """RACLlamaBlock's math in plain torch fp32 (interleaved RoPE, MHA)."""
-    a = blk.attn
-    H, hd = a.n_heads, a.d_head
-    B, T, d = x.shape
-
-    def rms(v, m):
-        return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + m.eps) * m.weight
-
-    q, k, v = (rms(x, blk.norm1) @ a.qkv.weight.T).chunk(3, -1)
-    q, k, v = (t.view(B, T, H, hd).transpose(1, 2) for t in (q, k, v))
-    c, s = a.rope.cos_cache[:T], a.rope.sin_cache[:T]
-
-    def rope(t):
-        t1, t2 = t[..., 0::2], t[..., 1::2]
-        return torch.stack([t1 * c - t2 * s, t1 * s + t2 * c], -1).flatten(-2)
-
-    o = F.scaled_dot_product_attention(rope(q), rope(k), v, is_causal=True)
-    h = x + o.transpose(1, 2).reshape(B, T, d) @ a.out_proj.weight.T
-    n = rms(h, blk.norm2)
-    f = blk.ffn
-    return h + (F.silu(n @ f.gate.weight.T) * (n @ f.up.weight.T)) @ f.down.weight.T
+    """The loaded block's math in plain torch fp32 (the oracle restatement)."""
+    from oracle import torch_block as TB
+    return TB.block_forward(TB.params_of(blk), x, blk.attn.n_heads, eps=blk.norm1.eps,
+                            cos=blk.attn.rope.cos_cache, sin=blk.attn.rope.sin_cache)
 
 
 def test_safetensors_round_trip(tmp_path):
