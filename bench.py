@@ -194,32 +194,38 @@ def cpu_stream_baseline(w: str, iters: int) -> dict | None:
         n = 1 << 22
         v = rng.standard_normal((n, 2)).astype(np.float32)
         th = rng.uniform(-np.pi, np.pi, n).astype(np.float32)
-        f = (lambda: O.ref_rotate_batch(v, th)) if iters == 16 else None
-        if f is None:
-            return None
-        units, unit, sample = n, "Gvec/s", f"2^22 vectors, lib/c rac_rotate_batch (16 iterations, OpenMP)"
+        if iters == 16:
+            f = lambda: O.ref_rotate_batch(v, th)                  # noqa: E731
+            kind, sample = "reference", "2^22 vectors, lib/c rac_rotate_batch (16 iterations, OpenMP)"
+        else:   # lib/c has only the scalar rac_rotate_n: time the OpenMP restatement of it
+            f = lambda: O.rotate_batch(v, th, iters, literal_kinv=False)   # noqa: E731
+            kind, sample = "port", f"2^22 vectors, rac_rotate_n restated (oracle, {iters} iterations, OpenMP)"
+        units, unit = n, "Gvec/s"
     elif w == "rope":
         x = rng.standard_normal((1, 32, 4096, 128)).astype(np.float32)
         c, s_ = O.ref_rope_cache(4096, 128, 10000.0)
         f = lambda: O.ref_rope_apply(x, c, s_)                    # noqa: E731
         units, unit, sample = x.size, "Gelem/s", "[1,32,4096,128], lib/c rac_rope_apply (incl. one copy)"
+        kind = "reference"
     elif w == "softmax":
         x = (rng.standard_normal((4096, 4096)) * 3).astype(np.float32)
         f = lambda: O.ref_softmax(x)                              # noqa: E731
         units, unit, sample = x.size, "Gelem/s", "4096 rows x 4096, lib/c rac_softmax_batch"
+        kind = "reference"
     else:
         x = rng.standard_normal((4096, 4096)).astype(np.float32)
         g = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
         b = (rng.standard_normal(4096) * 0.1).astype(np.float32)
         f = (lambda: O.ref_rmsnorm(x, g, 1e-6)) if w == "rmsnorm" else (lambda: O.ref_layernorm(x, g, b, 1e-6))
         units, unit, sample = x.size, "Gelem/s", f"4096 rows x 4096, lib/c rac_{w}"
+        kind = "reference"
     f()
     t0 = time.perf_counter()
     reps = 3
     for _ in range(reps):
         f()
     t = (time.perf_counter() - t0) / reps
-    return {"value": units / t / 1e9, "unit": unit, "cores": cores, "kind": "reference", "sample": sample}
+    return {"value": units / t / 1e9, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
 
 def cpu_llama_baseline(size: int) -> dict:

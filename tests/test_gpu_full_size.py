@@ -1,0 +1,77 @@
+"""Streaming ops at the full benchmark sizes, each compared element for element
+with the OpenMP restatement (which finishes these in seconds):
+
+* rac_rotate_batch_n over 2^26 vectors (N(0,1), theta U[-pi, pi)), 16 and 24
+  iterations: bit-exact;
+* rac_rope_apply on Q [8, 32, 4096, 128]: bit-exact;
+* rac_softmax_batch on [32768, 4096] ~N(0, 9): max relative error <= 1e-4;
+* rac_rmsnorm / rac_layernorm on [16384, 4096]: the reduction bars of the
+  reduced-size tests.
+
+Each call runs through the stream-ordered C ABI on device tensors, as the
+benchmark does.  Sizes and distributions follow the benchmark configs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from rac_b200 import ext
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _mismatches(a, b):
+    return int(np.count_nonzero(np.asarray(a, np.float32).view(np.uint32)
+                                != np.asarray(b, np.float32).view(np.uint32)))
+
+
+@pytest.mark.parametrize("it", [16, 24])
+def test_rotate_batch_2p26(cuda, orc, it):
+    rng = np.random.default_rng(100 + it)
+    n = 1 << 26
+    v = rng.standard_normal((n, 2), dtype=np.float32)
+    th = rng.uniform(-math.pi, math.pi, n).astype(np.float32)
+    got = ext.rotate_batch(_t(v, cuda), _t(th, cuda), it).cpu().numpy()
+    assert _mismatches(got, orc.rotate_batch(v, th, it, False)) == 0
+
+
+def test_rope_apply_full_q(cuda, orc):
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((8, 32, 4096, 128), dtype=np.float32)
+    c, s = orc.rope_cache(4096, 128, 10000.0)
+    xt = _t(x, cuda)
+    ext.rope_apply_(xt, _t(c, cuda), _t(s, cuda))
+    assert _mismatches(xt.cpu().numpy(), orc.rope_apply(x, c, s)) == 0
+
+
+def test_softmax_full(cuda, orc):
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((32768, 4096), dtype=np.float32) * 3
+    got = ext.softmax(_t(x, cuda)).cpu().numpy()
+    assert O.max_rel_err(got, orc.softmax(x)) <= 1e-4
+
+
+def test_norms_full(cuda, orc):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((16384, 4096), dtype=np.float32)
+    g = rng.uniform(0.5, 1.5, 4096).astype(np.float32)
+    b = (rng.standard_normal(4096) * 0.1).astype(np.float32)
+    xd = _t(x, cuda)
+    got = ext.rmsnorm(xd, _t(g, cuda), 1e-6).cpu().numpy()
+    assert O.max_rel_err(got, orc.rmsnorm(x, g, 1e-6)) <= 1e-4
+    got = ext.layernorm(xd, _t(g, cuda), _t(b, cuda), 1e-6).cpu().numpy()
+    rows = slice(0, 16384, 61)                 # float64 exact result on a row sample
+    xs = x[rows].astype(np.float64)
+    m = xs.mean(1, keepdims=True)
+    exact = g * (xs - m) / np.sqrt(((xs - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
+    want = orc.layernorm(x, g, b, 1e-6)
+    assert O.reduction_ok(got[rows], want[rows], exact)
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    assert float(np.abs(got - want).max()) / rms <= 1e-5           # normwise, every row
