@@ -139,32 +139,33 @@ __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
     return x;
 }
 
+// Bit pattern of 2^-i, i = 0..126.
+__host__ __device__ constexpr unsigned pow2neg_bits(int i) { return (unsigned)(127 - i) << 23; }
+
+// atan_i * 2^i (exact: a power-of-two scaling of a normal float).
+__host__ __device__ constexpr float atan_scaled(int i) {
+    float a = atan_entry(i);
+    for (int k = 0; k < i; ++k) a *= 2.0f;
+    return a;
+}
+
 // _cordic_rotate of lib/c/rac_cpu.c:90-118: wrap theta to (-pi, pi], fold
 // into [-pi/2, pi/2] by negating (x, y), then ITERS micro-rotations whose
 // direction d_i = (angle_i >= 0) ? +1 : -1 is the sign of the residual angle.
 // (x, y) arrive pre-scaled.  Returns false when the wrap loop hit kWrapLimit.
 //
-// Pipe balance: the direction of iterations i >= 1 is computed on the FMA
-// pipe, not with sign-bit logic on the (half-rate) ALU pipe:
-//   t_i = sat(angle_i * 2^126 + 1)          -> 1 if angle_i >= 0 (incl. -0),
-//                                              0 if angle_i < 0 or NaN
-//   d_i = 2 t_i - 1,  d_i * 2^-i and d_i * atan_i exact (d_i = +-1)
-// This equals the comparison whenever angle_i is 0 or |angle_i| >= 2^-125.
-// For i >= 1 that always holds: angle_1 = fl(angle_0 -+ atan_0) has
-// magnitude >= 2^-2 or is a difference of floats near atan_0 (a multiple of
-// 2^-25), and every later angle is a rounded sum of it and table entries,
-// hence 0 or a multiple of 2^-48.  Iteration 0 (arbitrary input angle,
-// possibly subnormal) uses the comparison itself.
-// sat(a * b + c) as one FFMA.SAT (PTX fma.rn.sat.f32: result clamped to
-// [0, 1], NaN -> +0).
-__device__ __forceinline__ float fma_sat(float a, float b, float c) {
-    float r;
-    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
+// Iteration 0 (arbitrary input angle, possibly -0 or subnormal) uses the
+// comparison itself; later iterations take the direction from the sign bit
+// (see the loop below).
 
+//
+// sign_mask must be 0x80000000.  A kernel that passes it in as a launch
+// argument keeps it in a register, so each direction below is one LOP3
+// ((angle & mask) | imm); with the literal default the compiler folds the
+// mask and needs two.
 template <int ITERS>
-__device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta) {
+__device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta,
+                                              unsigned sign_mask = 0x80000000u) {
     const float TAU = 2.0f * kPi;
     bool ok = true;
     int w = 0;
@@ -184,20 +185,30 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta)
         x = xn;
         if (ITERS > 1) angle = __fsub_rn(angle, d * atan_entry(0));
     }
-    // Each instruction below carries at most one immediate (FFMA encodes one);
-    // the +1 / -1 addends live in registers, so an iteration is exactly six
-    // FMA-pipe instructions with no constant materialisation.
-    const float one = 1.0f, neg_one = -1.0f;
+    // Iterations i >= 1: four instructions, one on the ALU pipe and three on
+    // the FMA pipe:
+    //   ds = (angle & sign) | bits(2^-i)          = d_i * 2^-i   (one LOP3)
+    //   x, y updated with ds                       (two FFMA)
+    //   angle - d_i*atan_i = fma(-ds, atan_i*2^i, angle): ds * (atan_i*2^i)
+    //   equals d_i*atan_i exactly (power-of-two scalings), and the FMA rounds
+    //   once, as the subtraction of the exact product does.  (one FFMA)
+    // The sign bit gives d_i = +1 exactly when angle_i >= 0: for i >= 1 the
+    // angle is a rounded difference with a nonzero table entry, so it is never
+    // -0; a NaN angle (NaN theta) must give d_i = -1 as the comparison does,
+    // and the FMA's NaN result is positive, so NaN is replaced by -inf, which
+    // stays -inf through every iteration.
+    if (ITERS > 1 && !(angle == angle)) angle = -INFINITY;
 #pragma unroll
     for (int i = 1; i < ITERS; ++i) {
-        const float t = fma_sat(angle, 0x1p126f, one);     // 1: angle >= 0, 0: < 0 / NaN
-        const float e = __fmaf_rn(t, 2.0f, neg_one);       // d_i = +-1
-        const float ds = __fmul_rn(e, pow2neg(i));          // d_i * 2^-i (exact)
+        unsigned dsb;
+        asm("lop3.b32 %0, %1, %2, %3, 0xEA;"           // (angle & sign_mask) | bits(2^-i)
+            : "=r"(dsb) : "r"(__float_as_uint(angle)), "r"(sign_mask), "r"(pow2neg_bits(i)));
+        const float ds = __uint_as_float(dsb);
         const float xn = __fmaf_rn(-ds, y, x);
         y = __fmaf_rn(ds, x, y);
         x = xn;
         if (i + 1 < ITERS)
-            angle = __fmaf_rn(-e, atan_entry(i), angle);    // angle - d_i*atan_i, one rounding
+            angle = __fmaf_rn(-ds, atan_scaled(i), angle);  // angle - d_i*atan_i, one rounding
     }
     xr = x; yr = y;
     return ok;

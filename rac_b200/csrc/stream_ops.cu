@@ -29,12 +29,15 @@ unsigned int* device_error_word(int device) {
     return w;
 }
 
+// Grid of a grid-stride kernel: 8 CTAs of 256 threads per SM.  For the
+// rotate kernels that is more than are resident at once (register-limited to
+// 6); the oversubscribed grid measured faster than one sized to occupancy.
 static int grid_for(long long work_items, int threads) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     long long blocks = (work_items + threads - 1) / threads;
-    long long cap = (long long)sms * 8;        // 8 resident 256-thread CTAs per SM
+    long long cap = (long long)sms * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     return (int)blocks;
@@ -45,8 +48,9 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 // ── rotate / project / sincos ────────────────────────────────────────────
 
 template <int ITERS>
-__device__ __forceinline__ bool rotate_one(float& x, float& y, float th, int iters) {
-    if constexpr (ITERS > 0) return cordic_rotate<ITERS>(x, y, th);
+__device__ __forceinline__ bool rotate_one(float& x, float& y, float th, int iters,
+                                           unsigned sign_mask) {
+    if constexpr (ITERS > 0) return cordic_rotate<ITERS>(x, y, th, sign_mask);
     else return cordic_rotate_rt(x, y, th, iters);
 }
 
@@ -56,7 +60,8 @@ template <int ITERS>
 __global__ void __launch_bounds__(256) k_rotate(const float2* __restrict__ v,
                                                 const float* __restrict__ th,
                                                 float2* __restrict__ out, long long n,
-                                                float k_inv, int iters, int vec) {
+                                                float k_inv, int iters, int vec,
+                                                unsigned sign_mask) {
     bool ok = true;
     const long long stride = (long long)gridDim.x * blockDim.x;
     long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -81,23 +86,23 @@ __global__ void __launch_bounds__(256) k_rotate(const float2* __restrict__ v,
             float x1 = __fmul_rn(v01.z, k_inv), y1 = __fmul_rn(v01.w, k_inv);
             float x2 = __fmul_rn(v23.x, k_inv), y2 = __fmul_rn(v23.y, k_inv);
             float x3 = __fmul_rn(v23.z, k_inv), y3 = __fmul_rn(v23.w, k_inv);
-            ok &= rotate_one<ITERS>(x0, y0, t.x, iters);
-            ok &= rotate_one<ITERS>(x1, y1, t.y, iters);
-            ok &= rotate_one<ITERS>(x2, y2, t.z, iters);
-            ok &= rotate_one<ITERS>(x3, y3, t.w, iters);
+            ok &= rotate_one<ITERS>(x0, y0, t.x, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x1, y1, t.y, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x2, y2, t.z, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x3, y3, t.w, iters, sign_mask);
             __stcs(reinterpret_cast<float4*>(out) + 2 * q, make_float4(x0, y0, x1, y1));
             __stcs(reinterpret_cast<float4*>(out) + 2 * q + 1, make_float4(x2, y2, x3, y3));
         }
         i0 += nq * 4;   // the scalar tail below covers [4*nq, n)
         for (long long i = i0; i < n; i += stride) {
             float x = __fmul_rn(v[i].x, k_inv), y = __fmul_rn(v[i].y, k_inv);
-            ok &= rotate_one<ITERS>(x, y, th[i], iters);
+            ok &= rotate_one<ITERS>(x, y, th[i], iters, sign_mask);
             out[i] = make_float2(x, y);
         }
     } else {
         for (long long i = i0; i < n; i += stride) {
             float x = __fmul_rn(v[i].x, k_inv), y = __fmul_rn(v[i].y, k_inv);
-            ok &= rotate_one<ITERS>(x, y, th[i], iters);
+            ok &= rotate_one<ITERS>(x, y, th[i], iters, sign_mask);
             out[i] = make_float2(x, y);
         }
     }
@@ -110,12 +115,12 @@ template <int ITERS>
 __global__ void __launch_bounds__(256) k_project(const float2* __restrict__ v,
                                                  const float* __restrict__ th,
                                                  float* __restrict__ out, long long n,
-                                                 float k_inv, int iters) {
+                                                 float k_inv, int iters, unsigned sign_mask) {
     bool ok = true;
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         float c = k_inv, s = 0.0f;
-        ok &= rotate_one<ITERS>(c, s, th[i], iters);
+        ok &= rotate_one<ITERS>(c, s, th[i], iters, sign_mask);
         const float2 a = v[i];
         out[i] = __fmaf_rn(a.x, c, __fmul_rn(a.y, s));
     }
@@ -142,7 +147,7 @@ static void launch_rotate_t(const float2* v, const float* th, float2* out, long 
                             float k_inv, int iters, cudaStream_t s) {
     const bool vec = al16(v) && al16(th) && al16(out);
     const int g = grid_for(vec ? (n + 3) / 4 : n, 256);
-    k_rotate<ITERS><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters, vec ? 1 : 0);
+    k_rotate<ITERS><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters, vec ? 1 : 0, 0x80000000u);
 }
 
 int rotate_batch(const float2* v, const float* th, float2* out, long long n, int iters,
@@ -169,12 +174,11 @@ int project_batch(const float2* v, const float* th, float* out, long long n, int
     if (!v || !th || !out) return kErrNullPtr;
     iters = iters < 4 ? 4 : (iters > 24 ? 24 : iters);
     const float k_inv = k_inv_of(iters);
-    const int g = grid_for(n, 256);
     switch (iters) {
-        case 8:  k_project<8><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters); break;
-        case 16: k_project<16><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters); break;
-        case 24: k_project<24><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters); break;
-        default: k_project<0><<<g, 256, 0, s>>>(v, th, out, n, k_inv, iters); break;
+        case 8:  k_project<8><<<grid_for(n, 256), 256, 0, s>>>(v, th, out, n, k_inv, iters, 0x80000000u); break;
+        case 16: k_project<16><<<grid_for(n, 256), 256, 0, s>>>(v, th, out, n, k_inv, iters, 0x80000000u); break;
+        case 24: k_project<24><<<grid_for(n, 256), 256, 0, s>>>(v, th, out, n, k_inv, iters, 0x80000000u); break;
+        default: k_project<0><<<grid_for(n, 256), 256, 0, s>>>(v, th, out, n, k_inv, iters, 0x80000000u); break;
     }
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
