@@ -18,8 +18,19 @@
 //
 // 128 threads: for the 64x64 score tile a thread owns rows rg + 16i (i < 4) and
 // columns cg + 8j (j < 8); for the 64 x HD output it owns the same rows and
-// HD/8 columns in float4 groups.  Shared rows are padded by 4 floats so that
-// the float4 reads of K, V and P are bank-conflict free.
+// HD/8 columns in float4 groups.  Shared memory holds Q, K and V tiles
+// (64 x HD each, unpadded) and the 64 x 64 P tile: 112 KB at HD = 128, so two
+// CTAs fit on an SM.  Bank conflicts are avoided by layout, not padding:
+//   * Q reads are broadcasts (the 8 threads of a quarter-warp share rg);
+//   * K is stored with its float4 column XORed by (row & 7), so the 8 rows a
+//     quarter-warp reads at one d fall in 8 different 16-byte bank groups;
+//   * V reads are 8 consecutive float4 of one row;
+//   * P is stored with its column XORed by (row & 3) << 3, so both the
+//     scalar writes (4 rows x 8 columns per warp) and the reads (4 rows, one
+//     column) hit distinct banks.
+// The K and V tiles stream in with cp.async while the previous phase
+// computes: V(kb) during the scores and softmax of tile kb, K(kb+1) during
+// P V of tile kb.
 #include <cmath>
 #include <mutex>
 
@@ -32,22 +43,41 @@ constexpr int kAttBQ = 64, kAttBK = 64, kAttThreads = 128;
 
 template <int HD>
 struct AttSmem {
-    static constexpr int LD = HD + 4;             // padded row (floats)
-    static constexpr int PLD = kAttBK + 4;
-    static constexpr size_t bytes = sizeof(float) * (2 * kAttBQ * LD + kAttBQ * PLD);
+    static_assert(HD % 32 == 0, "the K swizzle needs >= 8 float4 per row");
+    static constexpr int PLD = kAttBK;
+    static constexpr size_t bytes = sizeof(float) * (3 * kAttBQ * HD + kAttBQ * PLD);
 };
 
+// Float offset of element (row r, float4 column c4) of a swizzled K tile.
 template <int HD>
-__device__ __forceinline__ void load_tile(float* dst, const float* __restrict__ src, int row0,
-                                          int rows_valid) {
-    constexpr int LD = AttSmem<HD>::LD;
+__device__ __forceinline__ int k_off(int r, int c4) { return r * HD + ((c4 ^ (r & 7)) << 2); }
+// Float offset of element (row r, column c) of the swizzled P tile.
+__device__ __forceinline__ int p_off(int r, int c) { return r * kAttBK + (c ^ ((r & 3) << 3)); }
+
+// 16-byte asynchronous global->shared copy (cp.async.cg); a src size of 0
+// zero-fills the destination (rows past the end of the sequence).
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Issues the copies of rows [row0, row0 + 64) of a [seq, HD] matrix into a
+// tile (zeros past rows_valid) and commits them as one group.
+template <int HD, bool SWZ>
+__device__ __forceinline__ void load_tile_async(float* dst, const float* __restrict__ src, int row0,
+                                                int rows_valid) {
     constexpr int QPR = HD / 4;                   // float4 per row
     for (int e = threadIdx.x; e < kAttBQ * QPR; e += kAttThreads) {
-        const int r = e / QPR, c = (e % QPR) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (row0 + r < rows_valid) v = __ldg(reinterpret_cast<const float4*>(src + (long long)(row0 + r) * HD + c));
-        *reinterpret_cast<float4*>(dst + r * LD + c) = v;
+        const int r = e / QPR, c4 = e % QPR;
+        const bool ok = row0 + r < rows_valid;
+        const int o = SWZ ? k_off<HD>(r, c4) : r * HD + 4 * c4;
+        cp_async16(dst + o, src + (long long)(ok ? row0 + r : 0) * HD + 4 * c4, ok);
     }
+    cp_async_commit();
 }
 
 // Scores of this thread's 4 x 8 block for the key tile in Ks, after scale,
@@ -56,7 +86,6 @@ template <int HD>
 __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, const float* Ks,
                                             int t0, int s0, int seq, float scale, int causal,
                                             const float* __restrict__ mask) {
-    constexpr int LD = AttSmem<HD>::LD;
     const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -65,10 +94,12 @@ __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, 
 #pragma unroll 4
     for (int d = 0; d < HD; d += 4) {
         float4 q[4], k[8];
+        // rows cg + 8j all have (row & 7) == cg: one swizzled column for all j
+        const int kc = ((d >> 2) ^ cg) << 2;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * LD + d);
+        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * HD + d);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * LD + d);
+        for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * HD + kc);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -101,11 +132,12 @@ __global__ void __launch_bounds__(kAttThreads, 2)
 k_attention(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
             const float* __restrict__ mask, int causal, float* __restrict__ out, int heads, int seq,
             float scale) {
-    constexpr int LD = AttSmem<HD>::LD, PLD = AttSmem<HD>::PLD, CG = HD / 32;
+    constexpr int CG = HD / 32;
     extern __shared__ __align__(16) float smem[];
     float* Qs = smem;
-    float* KVs = Qs + kAttBQ * LD;
-    float* Ps = KVs + kAttBQ * LD;
+    float* Ks = Qs + kAttBQ * HD;
+    float* Vs = Ks + kAttBQ * HD;
+    float* Ps = Vs + kAttBQ * HD;
 
     const int nqb = (seq + kAttBQ - 1) / kAttBQ;
     const int qb = nqb - 1 - blockIdx.x;          // heaviest (causal) blocks first
@@ -118,7 +150,8 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
     const int nkb = causal ? min(qb + 1, (seq + kAttBK - 1) / kAttBK) : (seq + kAttBK - 1) / kAttBK;
 
-    load_tile<HD>(Qs, qh, t0, seq);
+    load_tile_async<HD, false>(Qs, qh, t0, seq);
+    load_tile_async<HD, true>(Ks, kh, 0, seq);
 
     // One pass with the running (online) row max m: per key tile,
     // m' = max(m, tile max), alpha = expf(m - m'), e = expf(s - m'),
@@ -131,11 +164,12 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
 #pragma unroll
         for (int g = 0; g < CG; ++g) o[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int kb = 0; kb < nkb; ++kb) {
-        __syncthreads();
-        load_tile<HD>(KVs, kh, kb * kAttBK, seq);
+        // V(kb) streams in during the scores and softmax of tile kb.
+        load_tile_async<HD, false>(Vs, vh, kb * kAttBK, seq);
+        cp_async_wait<1>();                       // Q and K(kb) have landed
         __syncthreads();
         float sc[4][8];
-        tile_scores<HD>(sc, Qs, KVs, t0, kb * kAttBK, seq, scale, causal, mask);
+        tile_scores<HD>(sc, Qs, Ks, t0, kb * kAttBK, seq, scale, causal, mask);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float tm = sc[i][0];
@@ -157,20 +191,26 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
             for (int j = 0; j < 8; ++j) {
                 const float e = (mn == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[i][j], mn));
                 lsum[i] = __fadd_rn(lsum[i], e);
-                Ps[(rg + 16 * i) * PLD + cg + 8 * j] = e;
+                Ps[p_off(rg + 16 * i, cg + 8 * j)] = e;
             }
         }
-        __syncthreads();
-        load_tile<HD>(KVs, vh, kb * kAttBK, seq);
+        __syncthreads();                          // P visible, K(kb) no longer read
+        // K(kb+1) streams in during P V of tile kb.
+        if (kb + 1 < nkb) {
+            load_tile_async<HD, true>(Ks, kh, (kb + 1) * kAttBK, seq);
+            cp_async_wait<1>();                   // V(kb) has landed
+        } else {
+            cp_async_wait<0>();
+        }
         __syncthreads();
         const int kmax = min(kAttBK, seq - kb * kAttBK);
         for (int s = 0; s < kmax; ++s) {
             float p[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = Ps[(rg + 16 * i) * PLD + s];
+            for (int i = 0; i < 4; ++i) p[i] = Ps[p_off(rg + 16 * i, s)];
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
-                const float4 vv = *reinterpret_cast<const float4*>(KVs + s * LD + cg * 4 + 32 * g);
+                const float4 vv = *reinterpret_cast<const float4*>(Vs + s * HD + cg * 4 + 32 * g);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     o[i][g].x = __fmaf_rn(p[i], vv.x, o[i][g].x);
@@ -180,6 +220,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
                 }
             }
         }
+        __syncthreads();                          // V and P free for the next tile
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
