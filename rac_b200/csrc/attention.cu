@@ -204,10 +204,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         }
         __syncthreads();
         const int kmax = min(kAttBK, seq - kb * kAttBK);
-        for (int s = 0; s < kmax; ++s) {
-            float p[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = Ps[p_off(rg + 16 * i, s)];
+        auto pv_key = [&](int s, const float (&p)[4]) {
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
                 const float4 vv = *reinterpret_cast<const float4*>(Vs + s * HD + cg * 4 + 32 * g);
@@ -219,6 +216,24 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
                     o[i][g].w = __fmaf_rn(p[i], vv.w, o[i][g].w);
                 }
             }
+        };
+        int s = 0;
+        // Four keys per P read: columns s..s+3 stay adjacent under the P
+        // swizzle (it flips bits 3-4 of the column), so one float4 per row.
+        for (; s + 4 <= kmax; s += 4) {
+            float4 p4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p4[i] = *reinterpret_cast<const float4*>(Ps + p_off(rg + 16 * i, s));
+            { const float p[4] = {p4[0].x, p4[1].x, p4[2].x, p4[3].x}; pv_key(s, p); }
+            { const float p[4] = {p4[0].y, p4[1].y, p4[2].y, p4[3].y}; pv_key(s + 1, p); }
+            { const float p[4] = {p4[0].z, p4[1].z, p4[2].z, p4[3].z}; pv_key(s + 2, p); }
+            { const float p[4] = {p4[0].w, p4[1].w, p4[2].w, p4[3].w}; pv_key(s + 3, p); }
+        }
+        for (; s < kmax; ++s) {
+            float p[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = Ps[p_off(rg + 16 * i, s)];
+            pv_key(s, p);
         }
         __syncthreads();                          // V and P free for the next tile
     }
