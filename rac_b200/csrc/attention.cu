@@ -21,9 +21,9 @@
 // HD/8 columns in float4 groups.  Shared memory holds Q, K and V tiles
 // (64 x HD each, unpadded) and the 64 x 64 P tile: 112 KB at HD = 128, so two
 // CTAs fit on an SM.  Bank conflicts are avoided by layout, not padding:
-//   * Q reads are broadcasts (the 8 threads of a quarter-warp share rg);
-//   * K is stored with its float4 column XORed by (row & 7), so the 8 rows a
-//     quarter-warp reads at one d fall in 8 different 16-byte bank groups;
+//   * Q and K are stored with their float4 column XORed by (row & 7): the 8
+//     K rows and the 4 Q rows a warp reads at one d fall in distinct 16-byte
+//     bank groups;
 //   * V reads are 8 consecutive float4 of one row;
 //   * P is stored with its column XORed by (row & 3) << 3, so both the
 //     scalar writes (4 rows x 8 columns per warp) and the reads (4 rows, one
@@ -48,7 +48,7 @@ struct AttSmem {
     static constexpr size_t bytes = sizeof(float) * (3 * kAttBQ * HD + kAttBQ * PLD);
 };
 
-// Float offset of element (row r, float4 column c4) of a swizzled K tile.
+// Float offset of element (row r, float4 column c4) of a swizzled Q or K tile.
 template <int HD>
 __device__ __forceinline__ int k_off(int r, int c4) { return r * HD + ((c4 ^ (r & 7)) << 2); }
 // Float offset of element (row r, column c) of the swizzled P tile.
@@ -94,10 +94,12 @@ __device__ __forceinline__ void tile_scores(float (&sc)[4][8], const float* Qs, 
 #pragma unroll 4
     for (int d = 0; d < HD; d += 4) {
         float4 q[4], k[8];
-        // rows cg + 8j all have (row & 7) == cg: one swizzled column for all j
+        // K rows cg + 8j all have (row & 7) == cg, Q rows rg + 16i have
+        // (row & 7) == (rg & 7): one swizzled column each for all j / i.
         const int kc = ((d >> 2) ^ cg) << 2;
+        const int qc = ((d >> 2) ^ (rg & 7)) << 2;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * HD + d);
+        for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (rg + 16 * i) * HD + qc);
 #pragma unroll
         for (int j = 0; j < 8; ++j) k[j] = *reinterpret_cast<const float4*>(Ks + (cg + 8 * j) * HD + kc);
 #pragma unroll
@@ -150,7 +152,7 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     const int rg = threadIdx.x >> 3, cg = threadIdx.x & 7;
     const int nkb = causal ? min(qb + 1, (seq + kAttBK - 1) / kAttBK) : (seq + kAttBK - 1) / kAttBK;
 
-    load_tile_async<HD, false>(Qs, qh, t0, seq);
+    load_tile_async<HD, true>(Qs, qh, t0, seq);
     load_tile_async<HD, true>(Ks, kh, 0, seq);
 
     // One pass with the running (online) row max m: per key tile,
