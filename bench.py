@@ -207,6 +207,12 @@ def cpu_stream_baseline(w: str, iters: int) -> dict | None:
         f = lambda: O.ref_rope_apply(x, c, s_)                    # noqa: E731
         units, unit, sample = x.size, "Gelem/s", "[1,32,4096,128], lib/c rac_rope_apply (incl. one copy)"
         kind = "reference"
+    elif w == "attention":
+        q, k, v = (rng.standard_normal((1, 8, 2048, 128)).astype(np.float32) for _ in range(3))
+        f = lambda: O.ref_attention(q, k, v, None, True)          # noqa: E731
+        units, unit = 2 * 8 * 2048 * 2048 * 128 * 1e-3, "TFLOP/s"   # /1e9 below -> TFLOP/s
+        sample = "[1,8,2048,128] causal, lib/c rac_scaled_dot_attention (OpenMP)"
+        kind = "reference"
     elif w == "softmax":
         x = (rng.standard_normal((4096, 4096)) * 3).astype(np.float32)
         f = lambda: O.ref_softmax(x)                              # noqa: E731
@@ -298,15 +304,17 @@ def run_reference(args) -> None:
 # ── GPU workloads ─────────────────────────────────────────────────────────
 
 def roofline_fp32(achieved_gops: float, iters: int, peaks: dict, sms: int, dur_ms: float,
-                  traffic) -> dict:
-    """FP32-issue roofline of the CORDIC GEMM: (2n+2) FP32 instructions per MAC
-    at SMs x 128 lanes x max SM clock (the cost model stated for the path)."""
+                  traffic, mode: int = 1) -> dict:
+    """FP32-issue roofline of the GEMM at SMs x 128 lanes x max SM clock:
+    CORDIC costs (2n+2) FP32 instructions per MAC (the cost model stated for
+    the path), FAST one FFMA per MAC."""
     mhz = float(peaks.get("sm_max_mhz", 1965.0))
     instr_peak = sms * 128 * mhz * 1e6
-    peak_gops = 2.0 * instr_peak / (2 * iters + 2) / 1e9
+    per_mac = (2 * iters + 2) if mode else 1
+    peak_gops = 2.0 * instr_peak / per_mac / 1e9
     return {"bound": "fp32_issue", "achieved": achieved_gops, "peak": peak_gops,
             "unit": "GOP/s (MAC-equiv)", "frac": achieved_gops / peak_gops,
-            "peak_basis": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz / {2 * iters + 2} instr per MAC "
+            "peak_basis": f"{sms} SMs x 128 FP32 lanes x {mhz:.0f} MHz / {per_mac} instr per MAC "
                           "(of measured sm_max_mhz)",
             "kernel_ms": dur_ms, "traffic": traffic}
 
@@ -390,7 +398,7 @@ def run_matmul(args, world, rank, local) -> dict | None:
         return None
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     peaks = load_peaks()
-    traffic = load_traffic().get(f"gemm_cordic{iters}_{M}")
+    traffic = load_traffic().get(f"gemm_cordic{iters}_{M}") if mode and M == N == K else None
     out = {
         "metric": "rac_matmul MAC-equiv GOP/s at 4096^3" if M == N == K == 4096
                   else f"rac_matmul MAC-equiv GOP/s at {M}x{N}x{K}",
@@ -401,7 +409,7 @@ def run_matmul(args, world, rank, local) -> dict | None:
                                f"{'CORDIC ' + str(iters) + ' iterations' if mode else 'FAST'}",
                    "sharding": f"N-columns over {world} rank(s), no collective",
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
-        "roofline": roofline_fp32(achieved_local, iters, peaks, sms, t_local, traffic),
+        "roofline": roofline_fp32(achieved_local, iters, peaks, sms, t_local, traffic, mode),
         "e2e": {"value": 2.0 * M * N * K / te / 1e9, "unit": "GOP/s",
                 "h2d_bytes_per_step": 4 * (M * K + K * Nl), "d2h_bytes_per_step": 4 * M * Nl,
                 "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"},
@@ -430,6 +438,70 @@ def _splits(M: int, N: int, K: int, sms: int) -> int:
         if share < best - 1e-9:
             best, S = share, c
     return S
+
+
+def stream_e2e(w: str, args, v: dict, world: int) -> dict:
+    """The workload through the blocking rac.h entry point with pinned HOST
+    buffers (host->device copies, kernel, device->host copies all inside the
+    wall-clock timed call), max over ranks."""
+    import ctypes
+
+    import torch
+    from rac_b200 import _lib
+    L = _lib.lib()
+    pin = lambda t: t.cpu().pin_memory()                      # noqa: E731
+    p = lambda t: t.data_ptr()                                # noqa: E731
+    f32 = ctypes.c_float
+    if w == "rotate":
+        vh, thh = pin(v["v"]), pin(v["th"])
+        oh = torch.empty_like(vh).pin_memory()
+        n = vh.shape[0]
+        call = lambda: L.rac_rotate_batch_n(p(vh), p(thh), p(oh), n, args.iters)  # noqa: E731
+        hin, hout = 12 * n, 8 * n
+    elif w == "rope":
+        qh, kh, ch, sh = pin(v["q"]), pin(v["kk"]), pin(v["ctab"]), pin(v["stab"])
+
+        def call():
+            L.rac_rope_apply(p(qh), p(ch), p(sh), *qh.shape)
+            L.rac_rope_apply(p(kh), p(ch), p(sh), *kh.shape)
+        hin = 4 * (qh.numel() + kh.numel()) + 2 * 4 * (ch.numel() + sh.numel())
+        hout = 4 * (qh.numel() + kh.numel())
+    elif w == "attention":
+        qh, kh, vh = pin(v["qa"]), pin(v["ka"]), pin(v["va"])
+        oh = torch.empty_like(qh).pin_memory()
+        B, H, T, D = qh.shape
+        call = lambda: L.rac_attention(p(qh), p(kh), p(vh), None, 1, p(oh), B, H, T, D)  # noqa: E731
+        hin, hout = 3 * 4 * qh.numel(), 4 * qh.numel()
+    else:
+        xh = pin(v["x"])
+        yh = torch.empty_like(xh).pin_memory()
+        rows, d = xh.shape
+        if w == "softmax":
+            call = lambda: L.rac_softmax_batch(p(xh), p(yh), rows, d)  # noqa: E731
+            hin = 4 * xh.numel()
+        elif w == "rmsnorm":
+            gh = pin(v["gam"])
+            call = lambda: L.rac_rmsnorm(p(xh), p(yh), p(gh), f32(1e-6), rows, d)  # noqa: E731
+            hin = 4 * (xh.numel() + d)
+        else:
+            gh, bh = pin(v["gam"]), pin(v["bet"])
+            call = lambda: L.rac_layernorm(p(xh), p(yh), p(gh), p(bh), f32(1e-6), rows, d)  # noqa: E731
+            hin = 4 * (xh.numel() + 2 * d)
+        hout = 4 * xh.numel()
+    call()
+    _lib.check()
+    ts = []
+    for _ in range(max(1, min(args.steps, 3))):
+        barrier(world)
+        t0 = time.perf_counter()
+        call()
+        ts.append(time.perf_counter() - t0)
+    _lib.check()
+    te = max_over_ranks(statistics.mean(ts), world)
+    units = v["units"]
+    val = units * world / te / (1e12 if w == "attention" else 1e9)
+    return {"value": val, "unit": v["unit_name"], "h2d_bytes_per_step": hin, "d2h_bytes_per_step": hout,
+            "api": "blocking rac.h call on pinned host buffers (C ABI)"}
 
 
 def run_stream(args, world, rank, local) -> dict | None:
@@ -502,6 +574,7 @@ def run_stream(args, world, rank, local) -> dict | None:
     barrier(world)
     t_local = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
     t = max_over_ranks(t_local, world)
+    e2e = stream_e2e(w, args, locals(), world)
     if rank != 0:
         return None
     peaks = load_peaks()
@@ -517,8 +590,10 @@ def run_stream(args, world, rank, local) -> dict | None:
                 "dtype": "f32", "data": "synthetic", "config": {"workload": cfg, "sharding": "replicas"},
                 "roofline": {"bound": "fp32", "achieved": flops, "peak": fp32, "unit": "TFLOP/s",
                              "frac": flops / fp32, "peak_basis": "SMs x 128 lanes x 2 x sm_max_mhz",
-                             "note": "the kernel executes 1.5x the algorithmic FLOPs (scores twice)"},
-                "gpu_launches": args.steps, "clocks": clk.summary()}
+                             "note": "causal diagonal tiles are computed in full (about 1/32 extra work)"},
+                "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+                "cpu_baseline": cpu_stream_baseline(w, args.iters)
+                if (world == 1 and not args.no_cpu_baseline) else None}
     cpu = cpu_stream_baseline(w, args.iters) if (world == 1 and not args.no_cpu_baseline) else None
     return {
         "cpu_baseline": cpu,
@@ -530,8 +605,8 @@ def run_stream(args, world, rank, local) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                      "frac": ach / peak, "peak_basis": "of measured" if "hbm_gbs" in peaks else "of fallback",
                      "frac_of_8TBs": ach / 8000.0, "kernel_ms": t_local,
-                     "traffic": load_traffic().get(f"{w}")},
-        "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
+                     "traffic": load_traffic().get(f"rotate_{args.iters}" if w == "rotate" else w)},
+        "e2e": e2e, "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
     }
 
 
