@@ -149,57 +149,54 @@ __host__ __device__ constexpr float atan_scaled(int i) {
     return a;
 }
 
-// _cordic_rotate of lib/c/rac_cpu.c:90-118: wrap theta to (-pi, pi], fold
-// into [-pi/2, pi/2] by negating (x, y), then ITERS micro-rotations whose
-// direction d_i = (angle_i >= 0) ? +1 : -1 is the sign of the residual angle.
-// (x, y) arrive pre-scaled.  Returns false when the wrap loop hit kWrapLimit.
+// _cordic_rotate of lib/c/rac_cpu.c:90-118 on (vx * kinv, vy * kinv): wrap
+// theta to (-pi, pi], fold into [-pi/2, pi/2] by negating (x, y), then ITERS
+// micro-rotations whose direction d_i = (angle_i >= 0) ? +1 : -1 is the sign
+// of the residual angle.  Returns false when the wrap loop hit kWrapLimit.
 //
-// Iteration 0 (arbitrary input angle, possibly -0 or subnormal) uses the
-// comparison itself; later iterations take the direction from the sign bit
-// (see the loop below).
-
+// Same roundings as the reference, fewer instructions:
+//  * the wrap loops run only when |theta| >= pi (NaN skips them, as there);
+//  * the fold's negation of (x, y) is folded into the scale: vx * -kinv is
+//    -(vx * kinv) exactly;
+//  * the fold's theta -/+ pi is theta + c with c = -copysign(pi, theta),
+//    which is the same rounded value; without a fold c = +0, which maps -0
+//    to +0 and leaves every other angle unchanged, so that the sign bit of
+//    the angle is the comparison angle >= 0 from iteration 0 on;
+//  * a NaN angle gives d_i = -1 in the reference (the comparison is false)
+//    and is replaced by -inf (fmaxf(NaN, -inf) = -inf), which stays -inf.
+// Each iteration is then four instructions, one on the ALU pipe and three on
+// the FMA pipe:
+//   ds = (angle & sign) | bits(2^-i)          = d_i * 2^-i   (one LOP3)
+//   x, y updated with ds                       (two FFMA)
+//   angle - d_i*atan_i = fma(-ds, atan_i*2^i, angle): ds * (atan_i*2^i)
+//   equals d_i*atan_i exactly (power-of-two scalings), and the FMA rounds
+//   once, as the subtraction of the exact product does.  (one FFMA)
+// For i >= 1 the angle is a rounded difference with a nonzero table entry,
+// so it is never -0 either.
 //
 // sign_mask must be 0x80000000.  A kernel that passes it in as a launch
-// argument keeps it in a register, so each direction below is one LOP3
+// argument keeps it in a register, so each direction is one LOP3
 // ((angle & mask) | imm); with the literal default the compiler folds the
 // mask and needs two.
 template <int ITERS>
-__device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta,
-                                              unsigned sign_mask = 0x80000000u) {
-    const float TAU = 2.0f * kPi;
+__device__ __forceinline__ bool cordic_rotate_scaled(float& xr, float& yr, float vx, float vy,
+                                                     float kinv, float theta,
+                                                     unsigned sign_mask = 0x80000000u) {
     bool ok = true;
-    int w = 0;
-    while (theta > kPi) { theta = __fsub_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
-    while (theta <= -kPi) { theta = __fadd_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
-    float x = xr, y = yr;
-    if (theta > kPi * 0.5f) {
-        x = -x; y = -y; theta = __fsub_rn(theta, kPi);
-    } else if (theta < -kPi * 0.5f) {
-        x = -x; y = -y; theta = __fadd_rn(theta, kPi);
+    if (fabsf(theta) >= kPi) {
+        const float TAU = 2.0f * kPi;
+        int w = 0;
+        while (theta > kPi) { theta = __fsub_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+        while (theta <= -kPi) { theta = __fadd_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
     }
-    float angle = theta;
-    {   // iteration 0: scale 1
-        const float d = (angle >= 0.0f) ? 1.0f : -1.0f;
-        const float xn = __fmaf_rn(-d, y, x);
-        y = __fmaf_rn(d, x, y);
-        x = xn;
-        if (ITERS > 1) angle = __fsub_rn(angle, d * atan_entry(0));
-    }
-    // Iterations i >= 1: four instructions, one on the ALU pipe and three on
-    // the FMA pipe:
-    //   ds = (angle & sign) | bits(2^-i)          = d_i * 2^-i   (one LOP3)
-    //   x, y updated with ds                       (two FFMA)
-    //   angle - d_i*atan_i = fma(-ds, atan_i*2^i, angle): ds * (atan_i*2^i)
-    //   equals d_i*atan_i exactly (power-of-two scalings), and the FMA rounds
-    //   once, as the subtraction of the exact product does.  (one FFMA)
-    // The sign bit gives d_i = +1 exactly when angle_i >= 0: for i >= 1 the
-    // angle is a rounded difference with a nonzero table entry, so it is never
-    // -0; a NaN angle (NaN theta) must give d_i = -1 as the comparison does,
-    // and the FMA's NaN result is positive, so NaN is replaced by -inf, which
-    // stays -inf through every iteration.
-    if (ITERS > 1 && !(angle == angle)) angle = -INFINITY;
+    const bool fold = fabsf(theta) > kPi * 0.5f;
+    const float c = fold ? __uint_as_float((~__float_as_uint(theta) & sign_mask) | __float_as_uint(kPi))
+                         : 0.0f;
+    float angle = fmaxf(__fadd_rn(theta, c), -INFINITY);
+    const float ks = fold ? -kinv : kinv;
+    float x = __fmul_rn(vx, ks), y = __fmul_rn(vy, ks);
 #pragma unroll
-    for (int i = 1; i < ITERS; ++i) {
+    for (int i = 0; i < ITERS; ++i) {
         unsigned dsb;
         asm("lop3.b32 %0, %1, %2, %3, 0xEA;"           // (angle & sign_mask) | bits(2^-i)
             : "=r"(dsb) : "r"(__float_as_uint(angle)), "r"(sign_mask), "r"(pow2neg_bits(i)));
@@ -212,6 +209,13 @@ __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta,
     }
     xr = x; yr = y;
     return ok;
+}
+
+// The same rotation of an already scaled (x, y).
+template <int ITERS>
+__device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta,
+                                              unsigned sign_mask = 0x80000000u) {
+    return cordic_rotate_scaled<ITERS>(xr, yr, xr, yr, 1.0f, theta, sign_mask);
 }
 
 // Runtime-iteration version of the same rotation (iters in [1, 24]).

@@ -47,11 +47,14 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 
 // ── rotate / project / sincos ────────────────────────────────────────────
 
+// (x, y) = rotation of (vx * k_inv, vy * k_inv) by th.
 template <int ITERS>
-__device__ __forceinline__ bool rotate_one(float& x, float& y, float th, int iters,
-                                           unsigned sign_mask) {
-    if constexpr (ITERS > 0) return cordic_rotate<ITERS>(x, y, th, sign_mask);
-    else return cordic_rotate_rt(x, y, th, iters);
+__device__ __forceinline__ bool rotate_one(float& x, float& y, float vx, float vy, float k_inv,
+                                           float th, int iters, unsigned sign_mask) {
+    if constexpr (ITERS > 0) return cordic_rotate_scaled<ITERS>(x, y, vx, vy, k_inv, th, sign_mask);
+    x = __fmul_rn(vx, k_inv);
+    y = __fmul_rn(vy, k_inv);
+    return cordic_rotate_rt(x, y, th, iters);
 }
 
 // out[i] = CORDIC rotation of (v[i] * k_inv) by theta[i]
@@ -82,27 +85,26 @@ __global__ void __launch_bounds__(256) k_rotate(const float2* __restrict__ v,
                 v23n = __ldcs(reinterpret_cast<const float4*>(v) + 2 * (q + stride) + 1);
                 tn = __ldcs(reinterpret_cast<const float4*>(th) + q + stride);
             }
-            float x0 = __fmul_rn(v01.x, k_inv), y0 = __fmul_rn(v01.y, k_inv);
-            float x1 = __fmul_rn(v01.z, k_inv), y1 = __fmul_rn(v01.w, k_inv);
-            float x2 = __fmul_rn(v23.x, k_inv), y2 = __fmul_rn(v23.y, k_inv);
-            float x3 = __fmul_rn(v23.z, k_inv), y3 = __fmul_rn(v23.w, k_inv);
-            ok &= rotate_one<ITERS>(x0, y0, t.x, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x1, y1, t.y, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x2, y2, t.z, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x3, y3, t.w, iters, sign_mask);
+            float x0, y0, x1, y1, x2, y2, x3, y3;
+            ok &= rotate_one<ITERS>(x0, y0, v01.x, v01.y, k_inv, t.x, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x1, y1, v01.z, v01.w, k_inv, t.y, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x2, y2, v23.x, v23.y, k_inv, t.z, iters, sign_mask);
+            ok &= rotate_one<ITERS>(x3, y3, v23.z, v23.w, k_inv, t.w, iters, sign_mask);
             __stcs(reinterpret_cast<float4*>(out) + 2 * q, make_float4(x0, y0, x1, y1));
             __stcs(reinterpret_cast<float4*>(out) + 2 * q + 1, make_float4(x2, y2, x3, y3));
         }
         i0 += nq * 4;   // the scalar tail below covers [4*nq, n)
         for (long long i = i0; i < n; i += stride) {
-            float x = __fmul_rn(v[i].x, k_inv), y = __fmul_rn(v[i].y, k_inv);
-            ok &= rotate_one<ITERS>(x, y, th[i], iters, sign_mask);
+            const float2 vi = v[i];
+            float x, y;
+            ok &= rotate_one<ITERS>(x, y, vi.x, vi.y, k_inv, th[i], iters, sign_mask);
             out[i] = make_float2(x, y);
         }
     } else {
         for (long long i = i0; i < n; i += stride) {
-            float x = __fmul_rn(v[i].x, k_inv), y = __fmul_rn(v[i].y, k_inv);
-            ok &= rotate_one<ITERS>(x, y, th[i], iters, sign_mask);
+            const float2 vi = v[i];
+            float x, y;
+            ok &= rotate_one<ITERS>(x, y, vi.x, vi.y, k_inv, th[i], iters, sign_mask);
             out[i] = make_float2(x, y);
         }
     }
@@ -119,8 +121,8 @@ __global__ void __launch_bounds__(256) k_project(const float2* __restrict__ v,
     bool ok = true;
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        float c = k_inv, s = 0.0f;
-        ok &= rotate_one<ITERS>(c, s, th[i], iters, sign_mask);
+        float c, s;
+        ok &= rotate_one<ITERS>(c, s, 1.0f, 0.0f, k_inv, th[i], iters, sign_mask);
         const float2 a = v[i];
         out[i] = __fmaf_rn(a.x, c, __fmul_rn(a.y, s));
     }
