@@ -310,52 +310,111 @@ RAC_API int rac_check_device_errors(void* stream) {
 // not depend on the row blocking, so the result equals one launch's, except
 // where a block's shape selects split-K (few output tiles, K >= 1024), whose
 // partial sums associate differently.
-static int matmul_pipelined(Call& c, const float* A, const float* dB, float* C, int M, int N, int K,
-                            int iters, int mode) {
-    thread_local std::vector<cudaStream_t> copy_streams;
-    if ((int)copy_streams.size() <= c.dev) copy_streams.resize(c.dev + 1, nullptr);
-    if (!copy_streams[c.dev] && cudaStreamCreateWithFlags(&copy_streams[c.dev], cudaStreamNonBlocking) != cudaSuccess)
-        return kErrCuda;
-    cudaStream_t cs = copy_streams[c.dev];
+static int sm_count_of(int dev) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) {
+        cudaGetLastError();
+        sms = 148;
+    }
+    return sms;
+}
+
+// Blocking rac_matmul with host A and C (and B on the host or the device):
+// C is computed in R row blocks so that copies overlap compute.  One stream
+// uploads B and then every row block of A; the compute stream runs each
+// block's GEMM as soon as its rows have landed; a third stream downloads each
+// C block as soon as it is done (PCIe is full duplex), so only B, the first
+// A block and the last C block are not hidden behind compute.  The caller
+// uses this path only when the whole problem would not split K, and the
+// blocks never split either, so every output is one GEMM over the whole of
+// K and the bits equal a single launch's.
+static int matmul_pipelined(Call& c, const float* A, const float* B, bool b_host, float* C, int M,
+                            int N, int K, int iters, int mode) {
+    struct Streams { cudaStream_t h2d = nullptr, d2h = nullptr; };
+    thread_local std::vector<Streams> per_dev;
+    if ((int)per_dev.size() <= c.dev) per_dev.resize(c.dev + 1);
+    Streams& ss = per_dev[c.dev];
+    for (cudaStream_t* q : {&ss.h2d, &ss.d2h})
+        if (!*q && cudaStreamCreateWithFlags(q, cudaStreamNonBlocking) != cudaSuccess) return kErrCuda;
+
     float* dA = nullptr;
+    float* dB = nullptr;
     float* dC = nullptr;
-    if (cudaMallocAsync(reinterpret_cast<void**>(&dA), sizeof(float) * (size_t)M * K, c.s) != cudaSuccess ||
-        cudaMallocAsync(reinterpret_cast<void**>(&dC), sizeof(float) * (size_t)M * N, c.s) != cudaSuccess) {
+    bool alloc_ok = cudaMallocAsync(reinterpret_cast<void**>(&dA), sizeof(float) * (size_t)M * K, c.s) == cudaSuccess &&
+                    cudaMallocAsync(reinterpret_cast<void**>(&dC), sizeof(float) * (size_t)M * N, c.s) == cudaSuccess;
+    if (alloc_ok && b_host)
+        alloc_ok = cudaMallocAsync(reinterpret_cast<void**>(&dB), sizeof(float) * (size_t)K * N, c.s) == cudaSuccess;
+    if (!alloc_ok) {
         cudaGetLastError();
         if (dA) cudaFreeAsync(dA, c.s);
+        if (dC) cudaFreeAsync(dC, c.s);
         return kErrAlloc;
     }
-    constexpr int kBlocks = 2;
-    cudaEvent_t ev[2 * kBlocks + 1];
-    for (auto& e : ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
-    // the copy stream may only write dA / dC after the allocations exist
-    cudaEventRecord(ev[2 * kBlocks], c.s);
-    cudaStreamWaitEvent(cs, ev[2 * kBlocks], 0);
+
+    // Four row blocks when each still fills the SMs several times over with
+    // 64 x 64 tiles, else two.
+    const long long block_tiles = (long long)((M / 4 + 63) / 64) * ((N + 63) / 64);
+    const int R = block_tiles >= 4LL * sm_count_of(c.dev) ? 4 : 2;
+    int rb[5];
+    for (int r = 0; r <= R; ++r) rb[r] = (int)((long long)M * r / R);
+
+    std::vector<cudaEvent_t> evs;
+    auto event = [&]() {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) evs.push_back(e);
+        return e;
+    };
     int st = kOk;
+    auto chk = [&](cudaError_t e) { if (e != cudaSuccess && st == kOk) st = kErrCuda; };
+
+    // Copy streams start after the allocations exist.
+    cudaEvent_t ev_alloc = event();
+    chk(cudaEventRecord(ev_alloc, c.s));
+    for (cudaStream_t q : {ss.h2d, ss.d2h}) chk(cudaStreamWaitEvent(q, ev_alloc, 0));
+    if (b_host)
+        chk(cudaMemcpyAsync(dB, B, sizeof(float) * (size_t)K * N, cudaMemcpyHostToDevice, ss.h2d));
+    cudaEvent_t ev_a[4];
+    for (int r = 0; r < R; ++r) {
+        const size_t off = (size_t)rb[r] * K;
+        if (rb[r + 1] > rb[r])
+            chk(cudaMemcpyAsync(dA + off, A + off, sizeof(float) * (size_t)(rb[r + 1] - rb[r]) * K,
+                                cudaMemcpyHostToDevice, ss.h2d));
+        ev_a[r] = event();
+        chk(cudaEventRecord(ev_a[r], ss.h2d));
+    }
+
     GemmParams p{};
-    p.B = dB; p.N = N; p.K = K; p.lda = K; p.ldb = N; p.ldc = N; p.ldcin = N;
+    p.B = b_host ? dB : B;
+    p.N = N; p.K = K; p.lda = K; p.ldb = N; p.ldc = N; p.ldcin = N;
     p.alpha = 1.0f; p.beta = 0.0f;
     p.iters = iters;
-    for (int r = 0; r < kBlocks && st == kOk; ++r) {
-        const int m0 = (int)((long long)M * r / kBlocks), m1 = (int)((long long)M * (r + 1) / kBlocks);
-        if (m1 <= m0) continue;
-        const size_t a_off = (size_t)m0 * K, c_off = (size_t)m0 * N;
-        if (cudaMemcpyAsync(dA + a_off, A + a_off, sizeof(float) * (size_t)(m1 - m0) * K,
-                            cudaMemcpyHostToDevice, cs) != cudaSuccess) { st = kErrCuda; break; }
-        cudaEventRecord(ev[2 * r], cs);
-        cudaStreamWaitEvent(c.s, ev[2 * r], 0);
-        p.A = dA + a_off; p.C = dC + c_off; p.Cin = p.C; p.M = m1 - m0;
-        st = launch_gemm(p, kNN, mode, 0, c.s);
-        cudaEventRecord(ev[2 * r + 1], c.s);
-        cudaStreamWaitEvent(cs, ev[2 * r + 1], 0);
-        if (st == kOk && cudaMemcpyAsync(C + c_off, dC + c_off, sizeof(float) * (size_t)(m1 - m0) * N,
-                                         cudaMemcpyDeviceToHost, cs) != cudaSuccess) st = kErrCuda;
+    for (int r = 0; r < R && st == kOk; ++r) {
+        if (rb[r + 1] <= rb[r]) continue;
+        chk(cudaStreamWaitEvent(c.s, ev_a[r], 0));
+        p.A = dA + (size_t)rb[r] * K;
+        p.C = dC + (size_t)rb[r] * N;
+        p.Cin = p.C;
+        p.M = rb[r + 1] - rb[r];
+        p.ws = nullptr; p.splits = 1; p.kchunk = 0;
+        if (st == kOk) st = launch_gemm_into(p, kNN, mode, 0, c.s);
+        cudaEvent_t done = event();
+        chk(cudaEventRecord(done, c.s));
+        chk(cudaStreamWaitEvent(ss.d2h, done, 0));
+        if (st == kOk)
+            chk(cudaMemcpyAsync(C + (size_t)rb[r] * N, p.C, sizeof(float) * (size_t)p.M * N,
+                                cudaMemcpyDeviceToHost, ss.d2h));
     }
-    if (cudaStreamSynchronize(cs) != cudaSuccess && st == kOk) st = kErrCuda;
-    // the frees are ordered after the copy stream's last use of dA / dC
+    // The frees on c.s are ordered after the copy streams' last use.
+    for (cudaStream_t q : {ss.h2d, ss.d2h}) {
+        cudaEvent_t e = event();
+        chk(cudaEventRecord(e, q));
+        chk(cudaStreamWaitEvent(c.s, e, 0));
+    }
     cudaFreeAsync(dA, c.s);
     cudaFreeAsync(dC, c.s);
-    for (auto& e : ev) cudaEventDestroy(e);
+    if (dB) cudaFreeAsync(dB, c.s);
+    if (cudaStreamSynchronize(c.s) != cudaSuccess && st == kOk) st = kErrCuda;
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
     return st;
 }
 
@@ -370,9 +429,12 @@ static int do_matmul(const float* A, const float* B, float* C, int M, int N, int
     mode = mode < 0 ? g_mode.load() : mode;
     const bool host_a = !is_device_ptr(A), host_c = !is_device_ptr(C);
     if (host_a && host_c && M >= 256) {
-        const float* dB = (const float*)c.map(B, sizeof(float) * (size_t)K * N, true, false);
-        const int st = c.st == kOk ? matmul_pipelined(c, A, dB, C, M, N, K, iters, mode) : c.st;
-        return c.finish(st, false);
+        GemmParams whole{};
+        whole.M = M; whole.N = N; whole.K = K;
+        if (splitk_count(whole, kNN, mode, 0) == 1) {
+            const int st = matmul_pipelined(c, A, B, !is_device_ptr(B), C, M, N, K, iters, mode);
+            return c.finish(st, false);
+        }
     }
     const float* dA = (const float*)c.map(A, sizeof(float) * (size_t)M * K, true, false);
     const float* dB = (const float*)c.map(B, sizeof(float) * (size_t)K * N, true, false);

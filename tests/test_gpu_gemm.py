@@ -244,12 +244,13 @@ def test_tma_staging_splitk_and_strided(cuda, orc):
     ext.check_device_errors()
 
 
-def test_rac_matmul_host_pipeline(cuda, orc):
-    """rac_matmul with host A and C runs the two-block copy/compute pipeline;
-    the result equals the restatement bit for bit (no split-K at this shape),
-    with B on the host or on the device."""
+@pytest.mark.parametrize("shape", [(1000, 512, 300), (300, 1100, 64), (257, 1030, 40), (2048, 2304, 64)])
+def test_rac_matmul_host_pipeline(cuda, orc, shape):
+    """rac_matmul with host A and C runs the row-block copy/compute pipeline
+    (2 or 4 blocks, ragged); the result equals the restatement bit for bit
+    (no split-K at these shapes), with B on the host or on the device."""
     L = _lib.lib()
-    M, N, K = 1000, 512, 300
+    M, N, K = shape
     A, B = _operands(M, N, K, "nn", 99)
     want = orc.gemm(A, B, "nn", 1, 16)
     for dev_b in (False, True):
