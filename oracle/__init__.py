@@ -31,8 +31,15 @@ class Vec2(C.Structure):
 
 
 def build() -> None:
-    """Compile liborc.so (and _ref when the reference sources exist)."""
+    """Compile liborc.so (and _ref when the reference sources exist; the
+    reference's CUDA extension only when it is not built yet, ~3 minutes)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if not os.path.exists(os.path.join(HERE, "_ref", "rac_cuda_ext.so")):
+        from . import build_ref_cuda
+        try:
+            build_ref_cuda.build()
+        except Exception as e:          # the parity test skips without it
+            print(f"oracle: reference CUDA extension not built: {e}")
 
 
 def _p(a: np.ndarray):
