@@ -10,7 +10,8 @@ F.linear), so its CPU path is:
   with the torch cos/sin cache                         (rac_torch.py:1132-1181)
 * softmax(Q K^T * hd^-0.5 + causal mask) V, out_proj   (rac_torch.py:1279-1343)
 * x + attn(RMS(x)); h + ffn(RMS(h))                   (rac_torch.py:1348-1383)
-* gated FFN  down(silu(gate x) * up x), the SwiGLU of
+* FFN: fc2(act(fc1 x)) (RACFusedFFN, rac_torch.py:631-655), or the gated
+  form down(silu(gate x) * up x), the SwiGLU of
   bench/bench_rac_transformer.c:441-453.
 """
 from __future__ import annotations
@@ -40,8 +41,8 @@ def _rope(t, c, s):
 
 def block_forward(p: dict, x: torch.Tensor, n_heads: int, eps: float = 1e-6,
                   cos=None, sin=None, causal: bool = True) -> torch.Tensor:
-    """p: {"norm1", "qkv", "out", "norm2", "gate", "up", "down"} fp32 tensors
-    (weights [out, in]).  x [B, T, d]."""
+    """p: {"norm1", "qkv", "out", "norm2"} plus {"gate", "up", "down"} (gated)
+    or {"fc1", "fc2"} (SiLU FFN): fp32 tensors, weights [out, in].  x [B, T, d]."""
     B, T, d = x.shape
     hd = d // n_heads
     if cos is None:
@@ -56,6 +57,8 @@ def block_forward(p: dict, x: torch.Tensor, n_heads: int, eps: float = 1e-6,
     o = torch.matmul(torch.softmax(scores, -1), v).transpose(1, 2).reshape(B, T, d)
     h = x + o @ p["out"].T
     n = _rms(h, p["norm2"], eps)
+    if "fc1" in p:
+        return h + F.silu(n @ p["fc1"].T) @ p["fc2"].T
     return h + (F.silu(n @ p["gate"].T) * (n @ p["up"].T)) @ p["down"].T
 
 

@@ -168,3 +168,23 @@ def test_attention_restatement_golden(orc, golden):
     q, k, v, m = golden["att_q"], golden["att_k"], golden["att_v"], golden["att_mask"]
     assert np.array_equal(orc.attention(q, k, v, None, True), golden["att_causal"])
     assert np.array_equal(orc.attention(q, k, v, m, False), golden["att_masked"])
+
+
+def test_torch_block_restatement_matches_reference_module(block_golden):
+    """oracle/torch_block.py against the reference RACLlamaBlock's own output
+    (CPU torch, seeded weights, tests/golden/rac_torch_block.npz)."""
+    import torch
+
+    from oracle import torch_block as TB
+    g = block_golden
+    d, H, ff, T, Bt, ms = [int(v) for v in g["cfg"]]
+    w = {k[2:]: torch.from_numpy(v) for k, v in g.items() if k.startswith("w.")}
+    p = {"norm1": w["norm1.weight"], "qkv": w["attn.qkv.weight"], "out": w["attn.out_proj.weight"],
+         "norm2": w["norm2.weight"], "fc1": w["ffn.fc1.weight"], "fc2": w["ffn.fc2.weight"]}
+    cos, sin = TB.rope_cache(d // H, ms)
+    x = torch.from_numpy(g["x"])
+    with torch.no_grad():
+        y = TB.block_forward(p, x, H, eps=1e-6, cos=cos, sin=sin, causal=True).numpy()
+        y_nc = TB.block_forward(p, x, H, eps=1e-6, cos=cos, sin=sin, causal=False).numpy()
+    assert np.abs(y - g["y"]).max() < 1e-5
+    assert np.abs(y_nc - g["y_noncausal"]).max() < 1e-5
