@@ -310,6 +310,113 @@ RAC_API int rac_check_device_errors(void* stream) {
 // not depend on the row blocking, so the result equals one launch's, except
 // where a block's shape selects split-K (few output tiles, K >= 1024), whose
 // partial sums associate differently.
+// Per-thread, per-device upload and download streams of the blocking calls.
+struct CopyStreams { cudaStream_t h2d = nullptr, d2h = nullptr; };
+static CopyStreams* copy_streams(int dev) {
+    thread_local std::vector<CopyStreams> per_dev;
+    if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+    CopyStreams& ss = per_dev[dev];
+    for (cudaStream_t* q : {&ss.h2d, &ss.d2h})
+        if (!*q && cudaStreamCreateWithFlags(q, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    return &ss;
+}
+
+// One argument of a chunked blocking call.  `unit` bytes per work unit for
+// arrays split with the work (vectors, rows, planes); unit == 0 marks an
+// array every chunk needs whole (gamma, tables, a mask) of `whole` bytes.
+// Device (or managed) pointers are used in place.
+struct Arg {
+    const void* host;
+    size_t unit, whole;
+    bool in, out;
+    char* dev = nullptr;
+    bool staged = false;
+};
+
+// Runs launch(u0, u1, stream) over [0, units) in chunks: with host arrays the
+// upload of chunk i+1 (one stream), the kernel of chunk i (the call stream)
+// and the download of chunk i-1 (another stream; PCIe is full duplex)
+// overlap.  Work units are independent, so chunking does not change any
+// result.  `align` keeps chunk starts on multiples of that many units.
+template <class Launch>
+static int run_chunked(Call& c, long long units, Arg* args, int nargs, long long align, Launch&& launch) {
+    size_t staged_bytes = 0;
+    for (int i = 0; i < nargs; ++i) {
+        Arg& a = args[i];
+        a.staged = a.host && !is_device_ptr(a.host);
+        a.dev = const_cast<char*>(static_cast<const char*>(a.host));
+        if (a.staged) staged_bytes += a.unit ? a.unit * (size_t)units : a.whole;
+    }
+    if (staged_bytes == 0) {                     // everything on the device already
+        const int st = launch(0LL, units, c.s);
+        return st;
+    }
+    CopyStreams* ss = copy_streams(c.dev);
+    if (!ss) return kErrCuda;
+    int st = kOk;
+    for (int i = 0; i < nargs && st == kOk; ++i) {
+        Arg& a = args[i];
+        if (!a.staged) continue;
+        const size_t bytes = a.unit ? a.unit * (size_t)units : a.whole;
+        void* d = nullptr;
+        if (cudaMallocAsync(&d, bytes, c.s) != cudaSuccess) { cudaGetLastError(); st = kErrAlloc; break; }
+        a.dev = static_cast<char*>(d);
+    }
+    std::vector<cudaEvent_t> evs;
+    auto event = [&]() {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) evs.push_back(e);
+        return e;
+    };
+    auto chk = [&](cudaError_t e) { if (e != cudaSuccess && st == kOk) st = kErrCuda; };
+    if (st == kOk) {
+        cudaEvent_t ev_alloc = event();
+        chk(cudaEventRecord(ev_alloc, c.s));
+        chk(cudaStreamWaitEvent(ss->h2d, ev_alloc, 0));
+        chk(cudaStreamWaitEvent(ss->d2h, ev_alloc, 0));
+        for (int i = 0; i < nargs; ++i)          // whole arrays first
+            if (args[i].staged && args[i].in && !args[i].unit)
+                chk(cudaMemcpyAsync(args[i].dev, args[i].host, args[i].whole, cudaMemcpyHostToDevice, ss->h2d));
+        // ~8 MiB of staged traffic per chunk, at most 16 chunks.
+        long long chunks = (long long)(staged_bytes >> 23);
+        chunks = chunks < 1 ? 1 : (chunks > 16 ? 16 : chunks);
+        long long per = (units + chunks - 1) / chunks;
+        per = (per + align - 1) / align * align;
+        for (long long u0 = 0; u0 < units && st == kOk; u0 += per) {
+            const long long u1 = u0 + per < units ? u0 + per : units;
+            for (int i = 0; i < nargs; ++i) {
+                const Arg& a = args[i];
+                if (a.staged && a.in && a.unit)
+                    chk(cudaMemcpyAsync(a.dev + a.unit * u0, static_cast<const char*>(a.host) + a.unit * u0,
+                                        a.unit * (u1 - u0), cudaMemcpyHostToDevice, ss->h2d));
+            }
+            cudaEvent_t in = event();
+            chk(cudaEventRecord(in, ss->h2d));
+            chk(cudaStreamWaitEvent(c.s, in, 0));
+            if (st == kOk) st = launch(u0, u1, c.s);
+            cudaEvent_t done = event();
+            chk(cudaEventRecord(done, c.s));
+            chk(cudaStreamWaitEvent(ss->d2h, done, 0));
+            for (int i = 0; i < nargs; ++i) {
+                const Arg& a = args[i];
+                if (a.staged && a.out && a.unit)
+                    chk(cudaMemcpyAsync(const_cast<char*>(static_cast<const char*>(a.host)) + a.unit * u0,
+                                        a.dev + a.unit * u0, a.unit * (u1 - u0), cudaMemcpyDeviceToHost, ss->d2h));
+            }
+        }
+        for (cudaStream_t q : {ss->h2d, ss->d2h}) {   // frees after the copies' last use
+            cudaEvent_t e = event();
+            chk(cudaEventRecord(e, q));
+            chk(cudaStreamWaitEvent(c.s, e, 0));
+        }
+    }
+    for (int i = 0; i < nargs; ++i)
+        if (args[i].staged && args[i].dev) cudaFreeAsync(args[i].dev, c.s);
+    if (cudaStreamSynchronize(c.s) != cudaSuccess && st == kOk) st = kErrCuda;
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
+    return st;
+}
+
 static int sm_count_of(int dev) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) {
@@ -330,12 +437,9 @@ static int sm_count_of(int dev) {
 // K and the bits equal a single launch's.
 static int matmul_pipelined(Call& c, const float* A, const float* B, bool b_host, float* C, int M,
                             int N, int K, int iters, int mode) {
-    struct Streams { cudaStream_t h2d = nullptr, d2h = nullptr; };
-    thread_local std::vector<Streams> per_dev;
-    if ((int)per_dev.size() <= c.dev) per_dev.resize(c.dev + 1);
-    Streams& ss = per_dev[c.dev];
-    for (cudaStream_t* q : {&ss.h2d, &ss.d2h})
-        if (!*q && cudaStreamCreateWithFlags(q, cudaStreamNonBlocking) != cudaSuccess) return kErrCuda;
+    CopyStreams* css = copy_streams(c.dev);
+    if (!css) return kErrCuda;
+    CopyStreams& ss = *css;
 
     float* dA = nullptr;
     float* dB = nullptr;
@@ -466,10 +570,12 @@ static int do_rotate(const float2* v, const float* th, float2* out, long long n,
     if (!v || !th || !out) return kErrNullPtr;
     Call c;
     if (c.begin() != kOk) return c.st;
-    auto dv = (const float2*)c.map(v, sizeof(float2) * n, true, false);
-    auto dt = (const float*)c.map(th, sizeof(float) * n, true, false);
-    auto dout = (float2*)c.map(out, sizeof(float2) * n, false, true);
-    int st = c.st == kOk ? rotate_batch(dv, dt, dout, n, iters, literal, c.s) : c.st;
+    Arg a[3] = {{v, sizeof(float2), 0, true, false}, {th, sizeof(float), 0, true, false},
+                {out, sizeof(float2), 0, false, true}};
+    const int st = run_chunked(c, n, a, 3, 64, [&](long long u0, long long u1, cudaStream_t s) {
+        return rotate_batch(reinterpret_cast<const float2*>(a[0].dev) + u0, reinterpret_cast<const float*>(a[1].dev) + u0,
+                            reinterpret_cast<float2*>(a[2].dev) + u0, u1 - u0, iters, literal, s);
+    });
     return c.finish(st, true);
 }
 
@@ -496,10 +602,12 @@ static int do_project(const float2* v, const float* th, float* out, long long n,
     if (!v || !th || !out) return kErrNullPtr;
     Call c;
     if (c.begin() != kOk) return c.st;
-    auto dv = (const float2*)c.map(v, sizeof(float2) * n, true, false);
-    auto dt = (const float*)c.map(th, sizeof(float) * n, true, false);
-    auto dout = (float*)c.map(out, sizeof(float) * n, false, true);
-    int st = c.st == kOk ? project_batch(dv, dt, dout, n, iters, c.s) : c.st;
+    Arg a[3] = {{v, sizeof(float2), 0, true, false}, {th, sizeof(float), 0, true, false},
+                {out, sizeof(float), 0, false, true}};
+    const int st = run_chunked(c, n, a, 3, 64, [&](long long u0, long long u1, cudaStream_t s) {
+        return project_batch(reinterpret_cast<const float2*>(a[0].dev) + u0, reinterpret_cast<const float*>(a[1].dev) + u0,
+                             reinterpret_cast<float*>(a[2].dev) + u0, u1 - u0, iters, s);
+    });
     return c.finish(st, true);
 }
 RAC_API void rac_project_batch_n(const float2* v, const float* theta, float* out, int n, int iters) {
@@ -517,9 +625,11 @@ static int do_unary(const float* x, float* y, long long n, int op) {
     if (!x || !y) return kErrNullPtr;
     Call c;
     if (c.begin() != kOk) return c.st;
-    auto dx = (const float*)c.map(x, sizeof(float) * n, true, false);
-    auto dy = (float*)c.map(y, sizeof(float) * n, false, true);
-    int st = c.st == kOk ? unary_batch(dx, dy, n, op, c.s) : c.st;
+    Arg a[2] = {{x, sizeof(float), 0, true, false}, {y, sizeof(float), 0, false, true}};
+    const int st = run_chunked(c, n, a, 2, 64, [&](long long u0, long long u1, cudaStream_t s) {
+        return unary_batch(reinterpret_cast<const float*>(a[0].dev) + u0, reinterpret_cast<float*>(a[1].dev) + u0,
+                           u1 - u0, op, s);
+    });
     return c.finish(st, false);
 }
 RAC_API void rac_exp_batch(const float* x, float* y, int n) { set_status(do_unary(x, y, n, kUnaryExp), "rac_exp_batch"); }
@@ -543,10 +653,13 @@ RAC_API void rac_sincos_batch(const float* theta, float* s, float* c_out, int n)
     else if (n > 0) {
         Call c;
         if (c.begin() == kOk) {
-            auto dt = (const float*)c.map(theta, sizeof(float) * n, true, false);
-            auto ds = (float*)c.map(s, sizeof(float) * n, false, true);
-            auto dc = (float*)c.map(c_out, sizeof(float) * n, false, true);
-            st = c.finish(c.st == kOk ? sincos_batch(dt, ds, dc, n, c.s) : c.st, true);
+            Arg a[3] = {{theta, sizeof(float), 0, true, false}, {s, sizeof(float), 0, false, true},
+                        {c_out, sizeof(float), 0, false, true}};
+            const int r = run_chunked(c, n, a, 3, 64, [&](long long u0, long long u1, cudaStream_t strm) {
+                return sincos_batch(reinterpret_cast<const float*>(a[0].dev) + u0, reinterpret_cast<float*>(a[1].dev) + u0,
+                                    reinterpret_cast<float*>(a[2].dev) + u0, u1 - u0, strm);
+            });
+            st = c.finish(r, true);
         } else {
             st = c.st;
         }
@@ -567,17 +680,18 @@ static int do_rows(int op, const float* x, float* y, const float* g, const float
     if (!x || !y) return kErrNullPtr;
     Call c;
     if (c.begin() != kOk) return c.st;
-    const size_t bytes = sizeof(float) * (size_t)rows * d;
-    auto dx = (const float*)c.map(x, bytes, true, false);
-    auto dy = (float*)c.map(y, bytes, false, true);
-    auto dg = (const float*)c.map(g, sizeof(float) * d, true, false);
-    auto db = (const float*)c.map(b, sizeof(float) * d, true, false);
-    int st = c.st;
-    if (st == kOk) {
-        if (op == 0) st = softmax_rows(dx, dy, rows, d, c.s);
-        else if (op == 1) st = rmsnorm_rows(dx, dy, dg, eps, rows, d, c.s);
-        else st = layernorm_rows(dx, dy, dg, db, eps, rows, d, c.s);
-    }
+    const size_t row = sizeof(float) * (size_t)d;
+    Arg a[4] = {{x, row, 0, true, false}, {y, row, 0, false, true},
+                {g, 0, row, true, false}, {b, 0, row, true, false}};
+    const int st = run_chunked(c, rows, a, 4, 1, [&](long long r0, long long r1, cudaStream_t s) {
+        const float* dx = reinterpret_cast<const float*>(a[0].dev) + r0 * d;
+        float* dy = reinterpret_cast<float*>(a[1].dev) + r0 * d;
+        const float* dg = reinterpret_cast<const float*>(a[2].dev);
+        const float* db = reinterpret_cast<const float*>(a[3].dev);
+        if (op == 0) return softmax_rows(dx, dy, r1 - r0, d, s);
+        if (op == 1) return rmsnorm_rows(dx, dy, dg, eps, r1 - r0, d, s);
+        return layernorm_rows(dx, dy, dg, db, eps, r1 - r0, d, s);
+    });
     return c.finish(st, false);
 }
 RAC_API void rac_softmax(float* x, float* out, int n) {
@@ -615,12 +729,14 @@ static int do_rope_apply(float* x, const float* ct, const float* sn, int batch, 
     if (batch <= 0 || heads <= 0 || seq <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidDim;
     Call c;
     if (c.begin() != kOk) return c.st;
-    const size_t xb = sizeof(float) * (size_t)batch * heads * seq * hd;
+    const size_t plane = sizeof(float) * (size_t)seq * hd;          // one (batch, head)
     const size_t tb = sizeof(float) * (size_t)seq * (hd / 2);
-    auto dx = (float*)c.map(x, xb, true, true);
-    auto dc = (const float*)c.map(ct, tb, true, false);
-    auto ds = (const float*)c.map(sn, tb, true, false);
-    int st = c.st == kOk ? rope_apply(dx, dc, ds, nullptr, (long long)batch * heads, seq, hd, 0, c.s) : c.st;
+    Arg a[3] = {{x, plane, 0, true, true}, {ct, 0, tb, true, false}, {sn, 0, tb, true, false}};
+    const int st = run_chunked(c, (long long)batch * heads, a, 3, 1,
+                               [&](long long p0, long long p1, cudaStream_t s) {
+        return rope_apply(reinterpret_cast<float*>(a[0].dev) + p0 * seq * hd, reinterpret_cast<const float*>(a[1].dev),
+                          reinterpret_cast<const float*>(a[2].dev), nullptr, p1 - p0, seq, hd, 0, s);
+    });
     return c.finish(st, false);
 }
 RAC_API void rac_rope_apply(float* x, const float* cos_tab, const float* sin_tab, int batch,
@@ -641,13 +757,18 @@ static int do_attention(const float* q, const float* k, const float* v, const fl
     if (batch <= 0 || heads <= 0 || seq <= 0 || hd <= 0) return kErrInvalidDim;
     Call c;
     if (c.begin() != kOk) return c.st;
-    const size_t bytes = sizeof(float) * (size_t)batch * heads * seq * hd;
-    auto dq = (const float*)c.map(q, bytes, true, false);
-    auto dk = (const float*)c.map(k, bytes, true, false);
-    auto dv = (const float*)c.map(v, bytes, true, false);
-    auto dm = (const float*)c.map(mask, sizeof(float) * (size_t)seq * seq, true, false);
-    auto dout = (float*)c.map(out, bytes, false, true);
-    int st = c.st == kOk ? attention(dq, dk, dv, dm, causal, dout, batch, heads, seq, hd, c.s) : c.st;
+    const size_t plane = sizeof(float) * (size_t)seq * hd;          // one (batch, head)
+    Arg a[5] = {{q, plane, 0, true, false}, {k, plane, 0, true, false}, {v, plane, 0, true, false},
+                {out, plane, 0, false, true}, {mask, 0, sizeof(float) * (size_t)seq * seq, true, false}};
+    const long long planes = (long long)batch * heads;
+    // Chunks hold whole batches (align = heads): each runs as (p1 - p0) / heads
+    // batches of `heads` heads, the launch shape of the whole call.
+    const int st = run_chunked(c, planes, a, 5, heads, [&](long long p0, long long p1, cudaStream_t s) {
+        const long long off = p0 * seq * hd;
+        return attention(reinterpret_cast<const float*>(a[0].dev) + off, reinterpret_cast<const float*>(a[1].dev) + off,
+                         reinterpret_cast<const float*>(a[2].dev) + off, reinterpret_cast<const float*>(a[4].dev),
+                         causal, reinterpret_cast<float*>(a[3].dev) + off, (int)((p1 - p0) / heads), heads, seq, hd, s);
+    });
     return c.finish(st, false);
 }
 RAC_API void rac_attention(const float* q, const float* k, const float* v, const float* mask,
