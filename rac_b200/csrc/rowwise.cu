@@ -48,21 +48,10 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
                                                          float eps, int d, long long rows) {
     __shared__ float red[kRowWarps];
     const int nq = d / 4;
-    // Persistent CTAs.  gamma / beta are staged once per CTA into shared
-    // memory (one L2 read per CTA, not per row), and the next row's loads are
-    // issued before the current row is reduced, so every CTA keeps one row of
-    // HBM reads in flight while it computes.
-    extern __shared__ float4 s_gb[];     // [nq] gamma, then [nq] beta
-    if constexpr (OP != kRowSoftmax) {
-        for (int q = threadIdx.x; q < nq; q += kRowThreads) {
-            s_gb[q] = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
-                            : make_float4(1.f, 1.f, 1.f, 1.f);
-            if constexpr (OP == kRowLayer)
-                s_gb[nq + q] = beta ? __ldg(reinterpret_cast<const float4*>(beta) + q)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        __syncthreads();
-    }
+    // One CTA per row (grid-stride if rows exceed the grid): the hardware
+    // overlaps rows across CTAs.  gamma / beta are read through the read-only
+    // path (L1 / L2 resident, 16 KB each at d = 4096); the loop issues the next
+    // row's loads before the current row is reduced when a CTA owns several.
     const float fd = (float)d;
     float4 nxt[V];
     auto load_row = [&](long long r) {
@@ -119,7 +108,8 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = s_gb[q];
+                const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
+                                       : make_float4(1.f, 1.f, 1.f, 1.f);
                 __stcs(yr + q, make_float4(__fmul_rn(__fmul_rn(v[j].x, inv), g.x),
                                            __fmul_rn(__fmul_rn(v[j].y, inv), g.y),
                                            __fmul_rn(__fmul_rn(v[j].z, inv), g.z),
@@ -151,8 +141,10 @@ __global__ void __launch_bounds__(kRowThreads) k_row_vec(const float* __restrict
         for (int j = 0; j < V; ++j) {
             const int q = threadIdx.x + j * kRowThreads;
             if (q < nq) {
-                const float4 g = s_gb[q];
-                const float4 b = s_gb[nq + q];
+                const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma) + q)
+                                       : make_float4(1.f, 1.f, 1.f, 1.f);
+                const float4 b = beta ? __ldg(reinterpret_cast<const float4*>(beta) + q)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 __stcs(yr + q, make_float4(
                     __fmaf_rn(g.x, __fmul_rn(__fsub_rn(v[j].x, mean), inv), b.x),
                     __fmaf_rn(g.y, __fmul_rn(__fsub_rn(v[j].y, mean), inv), b.y),
@@ -212,38 +204,15 @@ __global__ void __launch_bounds__(kRowThreads) k_row_any(const float* __restrict
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Grid = resident CTAs per SM x SMs (persistent; x 8 for RMSNorm), capped at
-// the row count.
+// One CTA per row.  Measured at [16384, 4096] against persistent CTAs that
+// staged gamma / beta in shared memory once: RMSNorm 0.0891 ms vs 0.0959
+// (persistent) / 0.0895 (8x oversubscribed), LayerNorm 0.0901 vs 0.0924;
+// softmax was already one CTA per row.
 template <int OP, int V>
 static void launch_vec(const float* x, float* y, const float* g, const float* b, float eps,
                        int d, long long rows, cudaStream_t s) {
-    const int nq = d / 4;
-    const size_t smem = OP == kRowSoftmax ? 0 : (OP == kRowLayer ? 2 : 1) * sizeof(float4) * nq;
-    // Occupancy depends on (device, smem bytes); cache the last answer per device.
-    static thread_local int c_dev = -1, c_sms = 0, c_per = 0;
-    static thread_local size_t c_smem = ~size_t(0);
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev != c_dev || smem != c_smem) {
-        cudaDeviceGetAttribute(&c_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(k_row_vec<OP, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c_per, k_row_vec<OP, V>, kRowThreads, smem);
-        if (c_per < 1) c_per = 1;
-        c_dev = dev; c_smem = smem;
-    }
-    const int sms = c_sms, per_sm = c_per;
-    // Softmax has no per-CTA state worth amortising: one CTA per row lets the
-    // hardware overlap rows across CTAs (measured faster than persistent).
-    // RMSNorm: 8 grid-stride CTAs per resident slot (the later CTAs fill SMs
-    // whose earlier CTAs finished): [16384, 4096] 0.0895 ms against 0.0959
-    // persistent.  LayerNorm stages gamma and beta (twice the shared bytes per
-    // CTA) and measured fastest persistent (0.0924 ms; 0.0984 ms at 8x).
-    constexpr int kMult = OP == kRowRms ? 8 : 1;
-    long long grid = OP == kRowSoftmax ? rows : (long long)per_sm * sms * kMult;
-    if (grid > rows) grid = rows;
-    if (grid > 0x7fffffffLL) grid = 0x7fffffffLL;
-    k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, smem, s>>>(x, y, g, b, eps, d, rows);
+    const long long grid = rows > 0x7fffffffLL ? 0x7fffffffLL : rows;
+    k_row_vec<OP, V><<<(unsigned)grid, kRowThreads, 0, s>>>(x, y, g, b, eps, d, rows);
 }
 
 template <int OP>
