@@ -88,30 +88,50 @@ class TPLlamaBlock(nn.Module):
     def forward(self, x, mask=None, is_causal=True, positions=None):
         res = x if self.rank == 0 else None
         ctx = self.attn._context(self.norm1(x), mask, is_causal, positions, n_heads=self.h_local)
-        h = self._allreduce(ext.linear_forward(ctx, self.attn.out_proj.weight, None,
-                                               residual=res, **_kw()))
+        h = self._allreduce(_apply(ctx, self.attn.out_proj, residual=res))
         n2 = self.norm2(h)
         res = h if self.rank == 0 else None
         if self.gated:
-            g = ext.linear_forward(n2, self.w_gate.weight, None, act=ext.ACT_SILU, **_kw())
-            u = ext.linear_forward(n2, self.w_up.weight, None, **_kw())
-            y = ext.linear_forward(g.mul_(u), self.w_down.weight, None, residual=res, **_kw())
+            g = _apply(n2, self.w_gate, act=ext.ACT_SILU)
+            u = _apply(n2, self.w_up)
+            y = _apply(g.mul_(u), self.w_down, residual=res)
         else:
-            t = ext.linear_forward(n2, self.w_fc1.weight, None, act=self.act_id, **_kw())
-            y = ext.linear_forward(t, self.w_fc2.weight, None, residual=res, **_kw())
+            t = _apply(n2, self.w_fc1, act=self.act_id)
+            y = _apply(t, self.w_fc2, residual=res)
         return self._allreduce(y)
 
 
 class _ShardLinear(nn.Module):
-    """A bias-free weight shard applied with the RAC GEMM (inference only)."""
+    """A bias-free weight shard applied with the RAC GEMM (inference only).
+
+    The shard is static, so it also keeps W^T (k-major): in FAST mode x W^T
+    runs as an NN GEMM on it, which measured faster than the NT form on this
+    GPU (4096^3: 3.05 against 3.66 ms) and gives the same bits (each output
+    still accumulates fma(x_k, w_k) over k in order)."""
 
     def __init__(self, w: torch.Tensor):
         super().__init__()
         self.weight = nn.Parameter(w.contiguous().clone(), requires_grad=False)
+        self.register_buffer("weight_t", w.t().contiguous().clone(), persistent=False)
         self.bias = None
 
     def forward(self, x):
-        return ext.linear_forward(x, self.weight, None, **_kw())
+        return _apply(x, self)
+
+
+def _apply(x: torch.Tensor, lin: _ShardLinear, act: int = ext.ACT_NONE,
+           residual: torch.Tensor | None = None) -> torch.Tensor:
+    """act(x W^T + residual) for a shard: NN on W^T in FAST mode, else NT on W."""
+    kw = _kw()
+    if kw["mode"] != ext.MODE_FAST:
+        return ext.linear_forward(x, lin.weight, None, act=act, residual=residual, **kw)
+    out_f, in_f = lin.weight.shape
+    shape = list(x.shape)
+    r2 = residual.reshape(-1, out_f) if residual is not None else None
+    out = ext.gemm(x.reshape(-1, in_f), lin.weight_t, ext.LAYOUT_NN, kw["iters"], kw["mode"],
+                   act=act, residual=r2)
+    shape[-1] = out_f
+    return out.reshape(shape)
 
 
 def _linear_from(w: torch.Tensor) -> nn.Module:
