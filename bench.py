@@ -1,7 +1,10 @@
 """Benchmark of the RAC rotation-accumulate hot path on B200.
 
 Default workload (the headline metric): rac_matmul, fp32 row-major
-M = N = K = 4096, A and B i.i.d. U[-1, 1), CORDIC mode, 16 iterations.
+M = N = K = 4096, A and B i.i.d. U[-1, 1), CORDIC mode, 16 iterations; the
+same JSON line carries the metric's second half under "llama":
+RACLlamaBlock tokens/s (d 4096, 32 heads, ff 11008 SwiGLU, x [4, 2048, 4096],
+CORDIC 16, tensor-parallel over the ranks).
 Metric: MAC-equivalent GOP/s = 2*M*N*K / t, summed over all ranks.  With N
 GPUs the columns of B and C are sharded across ranks (no collective on the
 data path; strong scaling of the fixed 4096^3 problem).
@@ -143,7 +146,7 @@ class ClockSampler:
 
 # ── CPU baselines (oracle/, the reference's lib/c built from its sources) ─
 
-def cpu_matmul_baseline(M: int, N: int, K: int, iters: int, reps: int = 1, warm: int = 1) -> dict:
+def cpu_matmul_baseline(M: int, N: int, K: int, iters: int, reps: int = 3, warm: int = 1) -> dict:
     """Times the reference's CPU rac_matmul (lib/c rac_hal_sgemm, AVX2 + OpenMP)
     on the full problem, plus the CORDIC GEMM composed from the reference's
     rac_project_n on a row sample (information only)."""
@@ -234,32 +237,102 @@ def cpu_stream_baseline(w: str, iters: int) -> dict | None:
     return {"value": units / t / 1e9, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
 
-def cpu_llama_baseline(size: int) -> dict:
-    """The reference RACLlamaBlock's CPU path (torch fp32 F.linear / matmul, which is
-    what the reference module runs off the GPU) on every host thread, on a bounded
-    sample: one sequence of 256 tokens through the full-width block."""
+class _RefSwiGLU:
+    """Built lazily around the reference module: down(silu(gate(x)) * up(x)) from
+    three reference RACLinear layers -- the SwiGLU of
+    bench/bench_rac_transformer.c:441-453, which the reference module lacks."""
+
+    @staticmethod
+    def make(ref, d, ff):
+        import torch.nn as nn
+        import torch.nn.functional as F
+
+        class RefSwiGLU(nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.gate = ref.RACLinear(d, ff, bias=False)
+                self.up = ref.RACLinear(d, ff, bias=False)
+                self.down = ref.RACLinear(ff, d, bias=False)
+
+            def forward(self, x):
+                return self.down(F.silu(self.gate(x)) * self.up(x))
+        return RefSwiGLU()
+
+
+def _load_reference_module():
+    """The reference's rac_torch.py (copied into oracle/_ref/py by oracle.build()),
+    imported WITHOUT an extension so that it runs its own CPU path."""
+    import importlib.util
+    import warnings
+    import oracle as O
+    path = os.path.join(O.REF_PY_DIR, "rac_torch_ref.py")
+    if not os.path.exists(path) or "rac_cuda_ext" in sys.modules:
+        return None
+    spec = importlib.util.spec_from_file_location("rac_torch_ref_cpu", path)
+    mod = importlib.util.module_from_spec(spec)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        spec.loader.exec_module(mod)
+    return mod
+
+
+def cpu_llama_baseline(sample: dict) -> dict:
+    """The reference RACLlamaBlock module on the host cores (every thread), on a
+    bounded sample: batch 0's first T tokens through the full-width block with
+    the benchmark's weights.  Off the GPU the reference module runs its own
+    torch fallback (F.linear / matmul, rac_torch.py:183, :232).  The FFN is the
+    gated one the benchmark runs, built from the reference's RACLinear.
+
+    Also checks the GPU output on that sample: causal attention makes the first
+    T outputs depend on the first T inputs only, so y_gpu[0, :T] must match the
+    CPU oracle (oracle/torch_block.py with the CORDIC operand map, the CORDIC
+    GEMM's exact identity) within 1e-4 of the output's rms."""
+    import numpy as np
     import torch
+    import oracle as O
     from oracle import torch_block as TB
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    d, H, ff = (4096, 32, 11008) if size == 4096 else (size, max(1, size // 128), int(size * 2.6875))
-    T = 256
-    g = torch.Generator().manual_seed(0)
-    w = lambda *shape: torch.randn(shape, generator=g) * 0.02          # noqa: E731
-    p = {"norm1": torch.ones(d), "qkv": w(3 * d, d), "out": w(d, d), "norm2": torch.ones(d),
-         "gate": w(ff, d), "up": w(ff, d), "down": w(d, ff)}
-    x = torch.randn((1, T, d), generator=g)
-    cos, sin = TB.rope_cache(d // H, T)
+    p, x, y_gpu, H = sample["params"], sample["x"], sample["y"], sample["heads"]
+    T, d = x.shape[1], x.shape[2]
+    ff = p["up"].shape[0]
+    iters = sample["iters"]
     with torch.no_grad():
-        TB.block_forward(p, x, H, cos=cos, sin=sin)
+        cos, sin = TB.rope_cache(d // H, T)
+        op = (lambda t: torch.from_numpy(O.cordic_operand(t.contiguous().numpy(), iters))) \
+            if sample["mode"] == "cordic" else None
+        want = TB.block_forward(p, x, H, cos=cos, sin=sin, operand=op).numpy()
+    err = float(np.abs(y_gpu.numpy() - want).max() / np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    assert err <= 1e-4, f"RACLlamaBlock output differs from the CPU oracle: {err:.3e}"
+    check = {"max_abs_over_rms": err, "bar": 1e-4,
+             "vs": f"oracle/torch_block.py ({sample['mode']}), batch 0 tokens 0..{T - 1}"}
+    ref = _load_reference_module()
+    with torch.no_grad():
+        if ref is not None:
+            blk = ref.RACLlamaBlock(d, H, ff_dim=ff, max_seq_len=T)
+            blk.ffn = _RefSwiGLU.make(ref, d, ff)
+            blk.norm1.weight.copy_(p["norm1"])
+            blk.norm2.weight.copy_(p["norm2"])
+            blk.attn.qkv.weight.copy_(p["qkv"])
+            blk.attn.out_proj.weight.copy_(p["out"])
+            for k in ("gate", "up", "down"):
+                getattr(blk.ffn, k).weight.copy_(p[k])
+            f = lambda: blk(x, is_causal=True)                 # noqa: E731
+            kind = "reference"
+            what = "the reference RACLlamaBlock module (rac_torch.py:1348-1383) on its CPU torch path"
+        else:
+            f = lambda: TB.block_forward(p, x, H, cos=cos, sin=sin)   # noqa: E731
+            kind = "port"
+            what = "oracle/torch_block.py, the restatement of the reference module's CPU path"
+        f()
         reps = 3
         t0 = time.perf_counter()
         for _ in range(reps):
-            TB.block_forward(p, x, H, cos=cos, sin=sin)
+            f()
         t = (time.perf_counter() - t0) / reps
-    return {"value": T / t, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"x [1,{T},{d}] through the gated block, torch fp32 on CPU "
-                      f"(the reference module's CPU path: F.linear/matmul, FMA not CORDIC)"}
+    return {"value": T / t, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"x [1,{T},{d}] through {what}, SwiGLU FFN, fp32 FMA (not CORDIC), mean of {reps}",
+            "parity_check": check}
 
 
 def run_reference(args) -> None:
@@ -633,6 +706,8 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=16384, help="norm workloads: row count")
     ap.add_argument("--log2n", type=int, default=26, help="rotate workload: log2 of the vector count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-llama", action="store_true",
+                    help="matmul workload: skip the RACLlamaBlock measurement in the same line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -641,11 +716,14 @@ def main() -> None:
         return
     _all_host_threads()
     world, rank, local = dist_init()
+    from rac_b200 import tp
+    llama = None
     if args.workload == "matmul":
         out = run_matmul(args, world, rank, local)
+        if not args.no_llama and args.size == 4096 and not args.shape:
+            llama = tp.bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     elif args.workload == "llama":
-        from rac_b200 import tp
-        out = tp.bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
+        out = llama = tp.bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     else:
         out = run_stream(args, world, rank, local)
     if rank == 0 and out is not None:
@@ -655,8 +733,12 @@ def main() -> None:
             else:
                 M = N = K = args.size
             out["cpu_baseline"] = cpu_matmul_baseline(M, N, K, args.iters)
-        if world == 1 and not args.no_cpu_baseline and args.workload == "llama":
-            out["cpu_baseline"] = cpu_llama_baseline(args.size)
+        if llama is not None:
+            sample = llama.pop("_sample", None)
+            if world == 1 and not args.no_cpu_baseline and sample is not None:
+                llama["cpu_baseline"] = cpu_llama_baseline(sample)
+            if llama is not out:
+                out["llama"] = llama
         print(json.dumps(out))
     if world > 1:
         import torch.distributed as dist

@@ -17,8 +17,9 @@
  * Declarations of the reference header that are outside the rotation-
  * accumulate hot path (rac_rotate_raw, rac_compensate, rac_project,
  * rac_polar, rac_norm, rac_normalize, rac_dot, rac_coherence,
- * rac_complex_mul, rac_dct, rac_inner, rac_outer, rac_attention) are not
- * exported.
+ * rac_complex_mul, rac_dct, rac_inner, rac_outer) are not exported.
+ * rac_attention (ref rac.h:330-335) is exported: the fused attention of the
+ * RACLlamaBlock path.
  */
 #ifndef RAC_H
 #define RAC_H

@@ -24,6 +24,13 @@
  *
  * Compile with nvcc -gencode arch=compute_100a,code=sm_100a and
  * -I<this directory>.
+ *
+ * Location: this header includes the library's internal device code
+ * (rac_b200/csrc/rac_device.cuh) by its path relative to this directory, so
+ * it compiles only from inside the source tree (or an install that keeps
+ * include/ and rac_b200/csrc/ side by side).  Only the rac_dev_* functions
+ * below are the public API; the racb:: names they use are internal and may
+ * change between versions.
  */
 #pragma once
 

@@ -30,10 +30,24 @@ class Vec2(C.Structure):
     _fields_ = [("x", C.c_float), ("y", C.c_float)]
 
 
+REF_PY_DIR = os.path.join(HERE, "_ref", "py")
+HIP_PATH = os.path.join(HERE, "_ref", "librac_hip_mac.so")
+
+
 def build() -> None:
-    """Compile liborc.so (and _ref when the reference sources exist; the
-    reference's CUDA extension only when it is not built yet, ~3 minutes)."""
+    """Compile liborc.so; where the reference checkout exists, also the reference's
+    lib/c (Makefile), its per-MAC HIP arithmetic as host code (build_ref_hip), a
+    copy of its Python module rac_torch.py under _ref/py/ (run on this library by
+    the drop-in test, and on the CPU as the block's timed baseline), and its CUDA
+    extension (only when not built yet, ~3 minutes)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
+    from . import build_ref_hip
+    build_ref_hip.build()
+    src = os.path.join(build_ref_hip.default_root(), "rac_torch", "rac_torch.py")
+    if os.path.exists(src):
+        import shutil
+        os.makedirs(REF_PY_DIR, exist_ok=True)
+        shutil.copyfile(src, os.path.join(REF_PY_DIR, "rac_torch_ref.py"))
     if not os.path.exists(os.path.join(HERE, "_ref", "rac_cuda_ext.so")):
         from . import build_ref_cuda
         try:
@@ -263,6 +277,69 @@ def gemm_composed_ref(A, B, iters: int = 16, rows=None):
     C_ = np.empty((r1 - r0, N), np.float32)
     fn = C.cast(ref().rac_project_n, C.c_void_p)
     orc().orc_gemm_composed_with(fn, _p(A), _p(B), _p(C_), M, N, K, iters, r0, r1)
+    return C_
+
+
+def cordic_operand(a, iters: int = 16):
+    """r(a) = round(x_n(a) * (1/K(n))) elementwise: the CORDIC-mode MAC is
+    fmaf(r(a), b, acc) exactly (the directions do not depend on the data and
+    the rotation is odd), so a CORDIC GEMM is a FAST GEMM of r(A) and B.
+    Computed as a 1x1 restated CORDIC GEMM against b = 1."""
+    a = _f32(a)
+    col = np.ascontiguousarray(a.reshape(-1, 1))
+    return gemm(col, np.ones((1, 1), np.float32), "nn", 1, iters).reshape(a.shape)
+
+
+# ── the reference's per-MAC HIP arithmetic, compiled as host code ─────────
+
+_hip = None
+
+
+def hip_available() -> bool:
+    return os.path.exists(HIP_PATH)
+
+
+def hip() -> C.CDLL:
+    """oracle/_ref/librac_hip_mac.so (built by build_ref_hip from rac_kernels.hip)."""
+    global _hip
+    if _hip is None:
+        lib = C.CDLL(HIP_PATH, mode=os.RTLD_LOCAL | os.RTLD_NOW)
+        I, F, L = C.c_int, C.c_float, C.c_long
+        lib.hipref_shiftadd_mul.argtypes = [F, F, I]
+        lib.hipref_shiftadd_mul.restype = F
+        lib.hipref_fma_cordic.argtypes = [F, F, F, I]
+        lib.hipref_fma_cordic.restype = F
+        lib.hipref_mac_batch.argtypes = [_fp, _fp, _fp, _fp, L, I, I]
+        lib.hipref_rotate_n.argtypes = [_fp, _fp, _fp, L, I]
+        lib.hipref_gemm.argtypes = [_fp, _fp, _fp, I, I, I, I, I, I]
+        _hip = lib
+    return _hip
+
+
+def hip_mac(a, b, acc, iters: int, mode: int):
+    """rac_fma_iters(a[i], b[i], acc[i], iters, mode) of rac_kernels.hip:202-218."""
+    a, b, acc = _f32(a), _f32(b), _f32(acc)
+    out = np.empty_like(a)
+    hip().hipref_mac_batch(_p(a), _p(b), _p(acc), _p(out), a.size, iters, mode)
+    return out
+
+
+def hip_rotate_n(v, theta, iters: int):
+    """rac_cordic_rotate_n of rac_kernels.hip:137-163 (no gain compensation)."""
+    v, theta = _f32(v), _f32(theta)
+    out = np.empty_like(v)
+    hip().hipref_rotate_n(_p(v), _p(theta), _p(out), theta.size, iters)
+    return out
+
+
+def hip_gemm(A, B, layout: str = "nn", mode: int = 1, iters: int = 16):
+    """Sequential-k GEMM over the reference's own rac_fma_iters."""
+    A, B = _f32(A), _f32(B)
+    lay = LAYOUTS[layout]
+    K, M = A.shape if lay == 2 else A.shape[::-1]
+    N = B.shape[0] if lay == 1 else B.shape[1]
+    C_ = np.empty((M, N), np.float32)
+    hip().hipref_gemm(_p(A), _p(B), _p(C_), M, N, K, lay, iters, mode)
     return C_
 
 

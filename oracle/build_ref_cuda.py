@@ -20,8 +20,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False) -> str | None:
-    src = os.path.join(ref_root, "rac_torch", "rac_torch.cu")
+def build(ref_root: str | None = None, verbose: bool = False) -> str | None:
+    from .build_ref_hip import default_root
+    src = os.path.join(ref_root or default_root(), "rac_torch", "rac_torch.cu")
     if not os.path.exists(src):
         return None
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")

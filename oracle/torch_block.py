@@ -40,32 +40,43 @@ def _rope(t, c, s):
 
 
 def block_forward(p: dict, x: torch.Tensor, n_heads: int, eps: float = 1e-6,
-                  cos=None, sin=None, causal: bool = True) -> torch.Tensor:
+                  cos=None, sin=None, causal: bool = True, operand=None) -> torch.Tensor:
     """p: {"norm1", "qkv", "out", "norm2"} plus {"gate", "up", "down"} (gated)
-    or {"fc1", "fc2"} (SiLU FFN): fp32 tensors, weights [out, in].  x [B, T, d]."""
+    or {"fc1", "fc2"} (SiLU FFN): fp32 tensors, weights [out, in].  x [B, T, d].
+
+    operand: a function applied to the activation operand of each of the four
+    projections before its product with the weight (None: identity).  With
+    oracle.cordic_operand it turns every projection into the CORDIC-mode GEMM
+    (CORDIC(A, W) == FAST(r(A), W) bit for bit), while the attention core stays
+    plain fp32 as in the reference module (rac_torch.py:1325-1337 uses
+    torch.matmul there)."""
+    op = operand or (lambda t: t)
     B, T, d = x.shape
     hd = d // n_heads
     if cos is None:
         cos, sin = rope_cache(hd, T)
     c, s = cos[:T], sin[:T]
-    q, k, v = (_rms(x, p["norm1"], eps) @ p["qkv"].T).chunk(3, -1)
+    q, k, v = (op(_rms(x, p["norm1"], eps)) @ p["qkv"].T).chunk(3, -1)
     q, k, v = (t.reshape(B, T, n_heads, hd).transpose(1, 2) for t in (q, k, v))
     q, k = _rope(q, c, s), _rope(k, c, s)
     scores = torch.matmul(q, k.transpose(-2, -1)) * hd ** -0.5
     if causal:
         scores = scores + torch.full((T, T), float("-inf")).triu(1)
     o = torch.matmul(torch.softmax(scores, -1), v).transpose(1, 2).reshape(B, T, d)
-    h = x + o @ p["out"].T
-    n = _rms(h, p["norm2"], eps)
+    h = x + op(o) @ p["out"].T
+    n = op(_rms(h, p["norm2"], eps))
     if "fc1" in p:
-        return h + F.silu(n @ p["fc1"].T) @ p["fc2"].T
-    return h + (F.silu(n @ p["gate"].T) * (n @ p["up"].T)) @ p["down"].T
+        return h + op(F.silu(n @ p["fc1"].T)) @ p["fc2"].T
+    return h + op(F.silu(n @ p["gate"].T) * (n @ p["up"].T)) @ p["down"].T
 
 
 def params_of(blk) -> dict:
-    """The restatement's parameter dict from a RACLlamaBlock(gated=True)."""
+    """The restatement's parameter dict from a RACLlamaBlock (gated or not)."""
     g = lambda t: t.detach().float().cpu()                      # noqa: E731
-    return {"norm1": g(blk.norm1.weight), "qkv": g(blk.attn.qkv.weight),
-            "out": g(blk.attn.out_proj.weight), "norm2": g(blk.norm2.weight),
-            "gate": g(blk.ffn.gate.weight), "up": g(blk.ffn.up.weight),
-            "down": g(blk.ffn.down.weight)}
+    p = {"norm1": g(blk.norm1.weight), "qkv": g(blk.attn.qkv.weight),
+         "out": g(blk.attn.out_proj.weight), "norm2": g(blk.norm2.weight)}
+    if hasattr(blk.ffn, "gate"):
+        p.update(gate=g(blk.ffn.gate.weight), up=g(blk.ffn.up.weight), down=g(blk.ffn.down.weight))
+    else:
+        p.update(fc1=g(blk.ffn.fc1.weight), fc2=g(blk.ffn.fc2.weight))
+    return p

@@ -471,8 +471,10 @@ class RACLlamaBlock(nn.Module):
 
 # ── model patching (rac_torch.py:865-942) ──────────────────────────────────
 
-def patch_model(model: nn.Module, min_features: int = 0, verbose: bool = True) -> nn.Module:
-    """Replaces every nn.Linear (in/out features >= min_features) by RACLinear."""
+def patch_model(model: nn.Module, verbose: bool = True, min_features: int = 64) -> nn.Module:
+    """Replaces every nn.Linear whose in and out features are both >= min_features
+    by RACLinear (same signature and default as rac_torch.py:865-869: layers
+    smaller than 64 stay torch's)."""
     count = 0
 
     def _replace(mod, prefix=""):

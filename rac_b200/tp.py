@@ -78,6 +78,18 @@ class TPLlamaBlock(nn.Module):
             self.w_fc1 = _linear_from(f.fc1.weight.data[f0:f1])
             self.w_fc2 = _linear_from(f.fc2.weight.data[:, f0:f1])
 
+    def full_params(self) -> dict:
+        """The block's weights as CPU fp32 tensors keyed norm1/qkv/out/norm2 and
+        gate/up/down (or fc1/fc2) -- the whole block only when world == 1."""
+        g = lambda t: t.detach().float().cpu()                  # noqa: E731
+        p = {"norm1": g(self.norm1.weight), "qkv": g(self.attn.qkv.weight),
+             "out": g(self.attn.out_proj.weight), "norm2": g(self.norm2.weight)}
+        if self.gated:
+            p.update(gate=g(self.w_gate.weight), up=g(self.w_up.weight), down=g(self.w_down.weight))
+        else:
+            p.update(fc1=g(self.w_fc1.weight), fc2=g(self.w_fc2.weight))
+        return p
+
     def _allreduce(self, t):
         if self.world > 1:
             import torch.distributed as dist
@@ -104,16 +116,28 @@ class TPLlamaBlock(nn.Module):
 class _ShardLinear(nn.Module):
     """A bias-free weight shard applied with the RAC GEMM (inference only).
 
-    The shard is static, so it also keeps W^T (k-major): in FAST mode x W^T
-    runs as an NN GEMM on it, which measured faster than the NT form on this
-    GPU (4096^3: 3.05 against 3.66 ms) and gives the same bits (each output
-    still accumulates fma(x_k, w_k) over k in order)."""
+    In FAST mode x W^T runs as an NN GEMM on a k-major copy W^T, which
+    measured faster than the NT form on this GPU (4096^3: 3.05 against
+    3.66 ms) and gives the same bits (each output still accumulates
+    fma(x_k, w_k) over k in order).  The copy is derived state: it is rebuilt
+    whenever the weight's storage or version counter changes (load_state_dict,
+    an in-place edit, a reassigned .data), so it can never go stale, and it
+    costs one more weight-sized buffer per shard while FAST mode is used."""
 
     def __init__(self, w: torch.Tensor):
         super().__init__()
         self.weight = nn.Parameter(w.contiguous().clone(), requires_grad=False)
-        self.register_buffer("weight_t", w.t().contiguous().clone(), persistent=False)
         self.bias = None
+        self._wt = None
+        self._wt_key = None
+
+    def weight_t(self) -> torch.Tensor:
+        w = self.weight
+        key = (w.data_ptr(), w._version, tuple(w.shape), w.device)
+        if self._wt is None or self._wt_key != key:
+            self._wt = w.detach().t().contiguous()
+            self._wt_key = key
+        return self._wt
 
     def forward(self, x):
         return _apply(x, self)
@@ -128,7 +152,7 @@ def _apply(x: torch.Tensor, lin: _ShardLinear, act: int = ext.ACT_NONE,
     out_f, in_f = lin.weight.shape
     shape = list(x.shape)
     r2 = residual.reshape(-1, out_f) if residual is not None else None
-    out = ext.gemm(x.reshape(-1, in_f), lin.weight_t, ext.LAYOUT_NN, kw["iters"], kw["mode"],
+    out = ext.gemm(x.reshape(-1, in_f), lin.weight_t(), ext.LAYOUT_NN, kw["iters"], kw["mode"],
                    act=act, residual=r2)
     shape[-1] = out_f
     return out.reshape(shape)
@@ -189,7 +213,7 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             starts[i].record(s)
-            blk(x)
+            y = blk(x)
             ends[i].record(s)
         torch.cuda.synchronize()
     launches = _lib.CALLS["n"] - calls0
@@ -211,6 +235,11 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     te = max_over_ranks(statistics.mean(ts), world)
     if rank != 0:
         return None
+    sample = None
+    if world == 1:       # batch 0, first 256 tokens: checked and timed on the CPU by bench.py
+        ts_ = min(T, 256)
+        sample = {"params": blk.full_params(), "x": x[:1, :ts_].cpu(), "y": y[:1, :ts_].cpu(),
+                  "heads": H, "mode": args.mode, "iters": args.iters}
     tokens = Bt * T
     macs = tokens * (4 * d * d + 3 * d * ff) // world            # projections, per rank
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -230,7 +259,8 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
         "e2e": {"value": tokens / te, "unit": "tokens/s", "h2d_bytes_per_step": 4 * x.numel(),
                 "d2h_bytes_per_step": 4 * x.numel()},
         "gpu_launches": launches,
-        "gpu_launches_note": "librac_b200 entry-point calls in the timed region (QK^T and PV use "
-                             "torch.matmul, as the reference module does)",
+        "gpu_launches_note": "librac_b200 entry-point calls in the timed region (projections, "
+                             "fused attention, RMSNorm, RoPE)",
         "clocks": clk.summary(),
+        "_sample": sample,
     }

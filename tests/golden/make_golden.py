@@ -104,9 +104,11 @@ def module_vectors(out: str, ref_root: str) -> None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", default=None,
+                    help="reference checkout (default: RAC_REF_ROOT, else ../reference beside the repo)")
     a = ap.parse_args()
     O.build()
     lib_vectors(os.path.join(HERE, "lib_c_vectors.npz"))
-    module_vectors(os.path.join(HERE, "rac_torch_block.npz"), a.ref_root)
+    from oracle.build_ref_hip import default_root
+    module_vectors(os.path.join(HERE, "rac_torch_block.npz"), a.ref_root or default_root())
     print("wrote", os.listdir(HERE))

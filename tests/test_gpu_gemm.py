@@ -179,6 +179,11 @@ def test_splitk_forced_with_epilogue(cuda, orc, layout):
     ref = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=1, **kw).cpu().numpy()
     got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 16, 1, variant=13, **kw).cpu().numpy()
     assert _normwise(got, ref) <= NORM_TOL
+    # and against the CPU oracle: silu(C_orc + R + bias), the epilogue's order
+    pre = torch.from_numpy(orc.gemm(A, B, layout, 1, 16)) + torch.from_numpy(R) + torch.from_numpy(bias)
+    want = torch.nn.functional.silu(pre).numpy()
+    assert _normwise(got, want) <= NORM_TOL
+    assert np.array_equal(ref, want) or _normwise(ref, want) <= 1e-6   # unsplit: same k order
 
 
 @pytest.mark.parametrize("variant", [1, 2, 3, 4])
@@ -276,3 +281,37 @@ def test_tma_wait_limit_reports_error_and_context_survives(cuda, orc):
     got = ext.gemm(dA, dB, LAYOUT_NN, 16, 1, variant=TMA).cpu().numpy()
     assert np.array_equal(got, orc.gemm(A, B, "nn", 1, 16))
     ext.check_device_errors()
+
+
+_EDGE = np.array([0.0, -0.0, 1.0, -1.0, 1e-40, -1e-40, 2.0 ** -126, -(2.0 ** -126), 1.5 * 2.0 ** -126,
+                  3e38, -3e38, 1e20, -1e20, 1e-20, 0.5, -0.75, 1e-30, 7.0, -123.456], np.float32)
+
+
+@pytest.mark.skipif(not O.hip_available(), reason="oracle/_ref/librac_hip_mac.so not built")
+@pytest.mark.parametrize("mode,iters", [(0, 24), (1, 4), (1, 8), (1, 16), (1, 24), (2, 8), (2, 24)])
+def test_gemm_bitexact_vs_reference_hip_code(cuda, mode, iters):
+    """Against the reference's own per-MAC code (rac_fma_iters of rac_kernels.hip,
+    compiled from the reference file as host code by oracle/build_ref_hip.py):
+    random operands in every layout, and every pair of edge values -- zeros,
+    subnormals, the smallest normals (where the fused micro-rotation matters),
+    huge values -- through a K = 1 GEMM of the edge column against the edge row
+    and a K = 2 GEMM that exercises the accumulation."""
+    rng = np.random.default_rng(mode * 31 + iters)
+    for layout in ("nn", "nt", "tn"):
+        A, B = _operands(70, 90, 150, layout, iters)
+        got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], iters, mode).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), O.hip_gemm(A, B, layout, mode, iters).view(np.uint32))
+    vals = np.concatenate([_EDGE, rng.standard_normal(13).astype(np.float32)])
+    col, row = vals.reshape(-1, 1).copy(), vals.reshape(1, -1).copy()
+    got = ext.gemm(_t(col, cuda), _t(row, cuda), LAYOUT_NN, iters, mode).cpu().numpy()
+    assert _same_bits(got, O.hip_gemm(col, row, "nn", mode, iters))
+    A2 = np.ascontiguousarray(np.stack([vals, vals[::-1]], 1))
+    B2 = np.ascontiguousarray(np.stack([vals[::-1], vals], 0))
+    got = ext.gemm(_t(A2, cuda), _t(B2, cuda), LAYOUT_NN, iters, mode).cpu().numpy()
+    assert _same_bits(got, O.hip_gemm(A2, B2, "nn", mode, iters))
+
+
+def _same_bits(x, y):
+    """Bit-equal, except that any NaN matches any NaN (the GPU's canonical NaN
+    and the host's differ in sign and payload)."""
+    return bool(((x.view(np.uint32) == y.view(np.uint32)) | (np.isnan(x) & np.isnan(y))).all())

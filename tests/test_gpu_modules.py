@@ -126,8 +126,10 @@ def test_patch_model(cuda, fast_mode):
     m = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.ReLU(), torch.nn.Linear(32, 8)).to(cuda)
     x = torch.randn(4, 16, device=cuda)
     ref = m(x)
-    R.patch_model(m, verbose=False)
-    assert isinstance(m[0], R.RACLinear)
+    R.patch_model(m, False)                 # reference signature: (model, verbose, min_features=64)
+    assert type(m[0]) is torch.nn.Linear and type(m[2]) is torch.nn.Linear
+    R.patch_model(m, verbose=False, min_features=8)
+    assert isinstance(m[0], R.RACLinear) and isinstance(m[2], R.RACLinear)
     assert torch.allclose(m(x), ref, atol=1e-5)
     R.unpatch_model(m, verbose=False)
     assert type(m[0]) is torch.nn.Linear
@@ -146,6 +148,22 @@ def test_tp_block_world1_equals_block(cuda, mode):
         assert torch.equal(y, y_tp)
     finally:
         R.rac_set_mode("fast")
+
+
+def test_tp_shard_transpose_follows_the_weight(cuda, fast_mode):
+    """The FAST-mode W^T of a tensor-parallel shard is derived state: an in-place
+    edit or a load_state_dict of the weight is seen by the next forward."""
+    lin = tp._ShardLinear(torch.randn(24, 40, device=cuda))
+    x = torch.randn(5, 40, device=cuda)
+    want = lambda: ext.linear_forward(x, lin.weight, None, iters=24, mode=0)   # noqa: E731
+    assert torch.equal(lin(x), want())
+    with torch.no_grad():
+        lin.weight.mul_(2)
+    assert torch.equal(lin(x), want())
+    lin.load_state_dict({"weight": torch.randn(24, 40, device=cuda)})
+    assert torch.equal(lin(x), want())
+    lin.weight.data = torch.randn(24, 40, device=cuda)
+    assert torch.equal(lin(x), want())
 
 
 def test_cpu_tensors_are_rejected():
