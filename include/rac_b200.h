@@ -40,6 +40,13 @@ extern "C" {
 #define RAC_ACT_RELU 1
 #define RAC_ACT_GELU 2
 #define RAC_ACT_SILU 3
+/* Gated FFN (SwiGLU, bench/bench_rac_transformer.c:441-453) in one GEMM: B holds
+ * the gate and up weights row-interleaved (gate row c at 2c, up row c at
+ * 2c+1), and C gets N/2 columns, C[m, c] = silu(v[m, 2c]) * v[m, 2c+1] with
+ * v = alpha * op(A) op(B) (+ bias).  N must be even and beta 0.  The same
+ * bits as a SiLU GEMM over the gate rows times a plain GEMM over the up rows,
+ * multiplied elementwise.  No counterpart in the reference's extension. */
+#define RAC_ACT_SWIGLU 4
 
 /* Thread-local status of the last call made on this thread (0 = ok). */
 int         rac_last_error(void);

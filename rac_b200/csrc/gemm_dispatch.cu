@@ -4,9 +4,22 @@
 #include <cudaTypedefs.h>
 #include <mutex>
 
-#include "gemm_kernel.cuh"
+#include "gemm_fast.cuh"
 
 namespace racb {
+
+RACB_FAST_TMA_EXTERN(kNN, 1) RACB_FAST_TMA_EXTERN(kTN, 1) RACB_FAST_TMA_EXTERN(kNN, 2) RACB_FAST_TMA_EXTERN(kTN, 2)
+
+// FAST mode, NN and TN on operands that meet the TMA rules and no split-K:
+// the TMA-staged FFMA2 kernel (gemm_fast.cuh), 64 x 128 tiles, or 128 x 128
+// when variant bit 0x2000 asks.  Everything else (NT, unaligned operands,
+// split-K, variant bit 0x400) runs the general kernel.
+static int pick_fast_tma(const GemmParams& p, int layout, int variant, cudaStream_t s) {
+    if (layout == kNT || p.ws || (variant & 0x400)) return kErrUnsupported;
+    if (variant & 0x2000)
+        return layout == kNN ? launch_fast_tma<kNN, 1>(p, s) : launch_fast_tma<kTN, 1>(p, s);
+    return layout == kNN ? launch_fast_tma<kNN, 2>(p, s) : launch_fast_tma<kTN, 2>(p, s);
+}
 
 #define E4(MODE, ITERS, LAY) RACB_GEMM_EXTERN(MODE, ITERS, LAY, 1, true) \
     RACB_GEMM_EXTERN(MODE, ITERS, LAY, 1, false) RACB_GEMM_EXTERN(MODE, ITERS, LAY, 3, true) \
@@ -203,6 +216,24 @@ int splitk_count(const GemmParams& p, int layout, int mode, int variant) {
 
 __global__ void __launch_bounds__(256) k_splitk_reduce(const GemmParams p) {
     const long long mn = (long long)p.M * p.N;
+    if (p.act == kActSwiGLU) {                  // one output per (gate, up) column pair
+        const int nh = p.N >> 1;
+        for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < mn / 2;
+             e += (long long)gridDim.x * blockDim.x) {
+            const int gm = (int)(e / nh), c = (int)(e % nh);
+            const long long e0 = (long long)gm * p.N + 2 * c;
+            float g = p.ws[e0], u = p.ws[e0 + 1];
+            for (int z = 1; z < p.splits; ++z) {
+                g = __fadd_rn(g, p.ws[z * mn + e0]);
+                u = __fadd_rn(u, p.ws[z * mn + e0 + 1]);
+            }
+            g = __fmul_rn(p.alpha, g);
+            u = __fmul_rn(p.alpha, u);
+            if (p.bias) { g = __fadd_rn(g, p.bias[2 * c]); u = __fadd_rn(u, p.bias[2 * c + 1]); }
+            p.C[(long long)gm * p.ldc + c] = __fmul_rn(apply_act(g, kActSilu), u);
+        }
+        return;
+    }
     for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < mn;
          e += (long long)gridDim.x * blockDim.x) {
         float acc = p.ws[e];
@@ -234,6 +265,7 @@ int launch_gemm(const GemmParams& p_in, int layout, int mode, int variant, cudaS
     if (!p_in.A || !p_in.B || !p_in.C) return kErrNullPtr;
     if (layout < kNN || layout > kTN) return kErrUnsupported;
     if (p_in.beta != 0.0f && !p_in.Cin) return kErrNullPtr;
+    if (p_in.act == kActSwiGLU && ((p_in.N & 1) || p_in.beta != 0.0f)) return kErrUnsupported;
     const int S = splitk_count(p_in, layout, mode, variant & 0xff);
     if (S <= 1) {
         GemmParams p = p_in;
@@ -278,7 +310,13 @@ int launch_gemm_into(const GemmParams& p_in, int layout, int mode, int variant, 
     const int b_contig = (layout == kNT) ? p.K : p.N;
     const bool vec = aligned16(p.A) && aligned16(p.B) && (p.lda % 4 == 0) &&
                      (p.ldb % 4 == 0) && (a_contig % 4 == 0) && (b_contig % 4 == 0);
-    if (mode == kFast) return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
+    if (mode == kFast) {
+        if (vec && v != 3) {
+            const int st = pick_fast_tma(p, layout, hooks, s);
+            if (st != kErrUnsupported) return st;
+        }
+        return pick_layout<kFast, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);
+    }
     if (mode == kShiftAdd) {
         if (p.iters < 1 || p.iters > kMaxIters) return kErrInvalidDim;
         return pick_layout<kShiftAdd, 0>(p, layout, (v == 2 || v == 4) ? 1 : v, vec, s);

@@ -126,6 +126,69 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 // lands sets bit 1 of the device error word instead of hanging the kernel.
 constexpr uint32_t kTmaWaitLimit = 1u << 22;
 
+// Writes a thread's TM x TN register tile: raw partial sums to the split-K
+// workspace, or the epilogue C = act(alpha*acc + beta*Cin + bias) (the
+// SwiGLU pairing included).  acc(i, j) reads the thread's accumulator,
+// row_of / col_of map tile indices to the CTA tile.
+template <int TM, int TN, class AccF, class RowF, class ColF>
+__device__ __forceinline__ void store_tile(const GemmParams& p, int m0, int n0, AccF acc,
+                                           RowF row_of, ColF col_of) {
+    if (p.ws) {   // split-K partial: raw sums, the reduction applies the epilogue
+        float* w = p.ws + (long long)blockIdx.z * p.M * p.N;
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int gm = m0 + row_of(i);
+            if (gm >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; ++j) {
+                const int gn = n0 + col_of(j);
+                if (gn < p.N) w[(long long)gm * p.N + gn] = acc(i, j);
+            }
+        }
+        return;
+    }
+    // Epilogue (rac_kernels.hip:790-797 for alpha/beta; rac_torch.cu:769-776
+    // for bias + activation).
+    if (p.act == kActSwiGLU) {
+        // Columns (2c, 2c+1) hold gate and up of output c; a thread's columns
+        // come in groups of 4 consecutive ones starting at a multiple of 4, so
+        // each pair is in one thread.  silu(gate) * up, each factor rounded as
+        // the separate GEMM epilogue and the elementwise product would round it.
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int gm = m0 + row_of(i);
+            if (gm >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; j += 2) {
+                const int gn = n0 + col_of(j);
+                if (gn >= p.N) continue;
+                float g = __fmul_rn(p.alpha, acc(i, j)), u = __fmul_rn(p.alpha, acc(i, j + 1));
+                if (p.bias) { g = __fadd_rn(g, p.bias[gn]); u = __fadd_rn(u, p.bias[gn + 1]); }
+                p.C[(long long)gm * p.ldc + (gn >> 1)] = __fmul_rn(apply_act(g, kActSilu), u);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int gm = m0 + row_of(i);
+        if (gm >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            const int gn = n0 + col_of(j);
+            if (gn >= p.N) continue;
+            float v;
+            if (p.beta != 0.0f)
+                v = __fmaf_rn(p.alpha, acc(i, j), __fmul_rn(p.beta, p.Cin[(long long)gm * p.ldcin + gn]));
+            else
+                v = __fmul_rn(p.alpha, acc(i, j));
+            if (p.bias) v = __fadd_rn(v, p.bias[gn]);
+            if (p.act) v = apply_act(v, p.act);
+            p.C[(long long)gm * p.ldc + gn] = v;
+        }
+    }
+}
+
 template <int MODE, int ITERS, int LAYOUT, int BM, int BN, int BK, int TM, int TN, bool VEC,
           int MINB = 1, bool TMA = false>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN), MINB)
@@ -287,40 +350,7 @@ k_gemm(const __grid_constant__ GemmParams p) {
         }
     }
 
-    if (p.ws) {   // split-K partial: raw sums, the reduction applies the epilogue
-        float* w = p.ws + (long long)blockIdx.z * p.M * p.N;
-#pragma unroll
-        for (int i = 0; i < TM; ++i) {
-            const int gm = m0 + row_of(i);
-            if (gm >= p.M) continue;
-#pragma unroll
-            for (int j = 0; j < TN; ++j) {
-                const int gn = n0 + col_of(j);
-                if (gn < p.N) w[(long long)gm * p.N + gn] = acc[i][j];
-            }
-        }
-        return;
-    }
-    // Epilogue (rac_kernels.hip:790-797 for alpha/beta; rac_torch.cu:769-776
-    // for bias + activation).
-#pragma unroll
-    for (int i = 0; i < TM; ++i) {
-        const int gm = m0 + row_of(i);
-        if (gm >= p.M) continue;
-#pragma unroll
-        for (int j = 0; j < TN; ++j) {
-            const int gn = n0 + col_of(j);
-            if (gn >= p.N) continue;
-            float v;
-            if (p.beta != 0.0f)
-                v = __fmaf_rn(p.alpha, acc[i][j], __fmul_rn(p.beta, p.Cin[(long long)gm * p.ldcin + gn]));
-            else
-                v = __fmul_rn(p.alpha, acc[i][j]);
-            if (p.bias) v = __fadd_rn(v, p.bias[gn]);
-            if (p.act) v = apply_act(v, p.act);
-            p.C[(long long)gm * p.ldc + gn] = v;
-        }
-    }
+    store_tile<TM, TN>(p, m0, n0, [&](int i, int j) { return acc[i][j]; }, row_of, col_of);
 }
 
 // Tile variants.  1: 64x128 CTA tile, 8x8 per thread (the general case);

@@ -10,7 +10,10 @@ namespace racb {
 
 enum Layout : int { kNN = 0, kNT = 1, kTN = 2 };
 enum Mode : int { kFast = 0, kCordic = 1, kShiftAdd = 2 };
-enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActSilu = 3 };
+// kActSwiGLU pairs adjacent output columns: C[m, c] = silu(v[m, 2c]) * v[m, 2c+1]
+// (C has N/2 columns) -- the gated FFN's gate and up projections as one GEMM
+// over row-interleaved weights.
+enum Act : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActSilu = 3, kActSwiGLU = 4 };
 
 // Status codes: lib/c/rac_cpu.h:54-59 plus the GPU-side ones.
 enum Status : int {

@@ -205,7 +205,7 @@ RAC_API int rac_gemm_async(const float* A, long long lda, const float* B, long l
     p.lda = lda; p.ldb = ldb; p.ldc = ldc; p.ldcin = Cin ? ldcin : ldc;
     p.alpha = alpha; p.beta = beta; p.act = act;
     p.iters = clamp_gemm_iters(iters);
-    if (act < kActNone || act > kActSilu) return set_status(kErrUnsupported, "rac_gemm_async");
+    if (act < kActNone || act > kActSwiGLU) return set_status(kErrUnsupported, "rac_gemm_async");
     if (M == 0 || N == 0) return set_status(kOk, "rac_gemm_async");
     return set_status(launch_gemm(p, layout, mode, variant, as_stream(stream)), "rac_gemm_async");
 }

@@ -24,6 +24,8 @@ from ._lib import LAYOUT_NN, LAYOUT_NT, LAYOUT_TN
 
 MODE_FAST, MODE_CORDIC, MODE_SHIFTADD = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_SILU = 0, 1, 2, 3
+# silu(v[:, 2c]) * v[:, 2c+1] over row-interleaved gate/up weights (N/2 outputs)
+ACT_SWIGLU = 4
 
 # Process-wide knobs of the torch binding (rac_torch_bind.cpp:54-55):
 # defaults iters = 24, mode = FAST.
@@ -100,8 +102,12 @@ def gemm(A: torch.Tensor, B: torch.Tensor, layout: int = LAYOUT_NN, iters: int =
     Kb = B.shape[1] if layout == LAYOUT_NT else B.shape[0]
     if Kb != K:
         raise ValueError(f"gemm: inner dimensions differ ({K} vs {Kb})")
+    if act == ACT_SWIGLU:
+        if N % 2 or residual is not None or (beta or 0.0) != 0.0:
+            raise ValueError("gemm: SwiGLU needs an even N and no residual")
     if out is None:
-        out = torch.empty((M, N), device=A.device, dtype=torch.float32)
+        out = torch.empty((M, N // 2 if act == ACT_SWIGLU else N), device=A.device,
+                          dtype=torch.float32)
     if residual is not None:
         residual = _f32(residual)
         if residual.stride(-1) != 1:
@@ -160,7 +166,7 @@ def linear_forward(input, weight, bias, iters=0, mode=-1, act: int = ACT_NONE,
     out = gemm(x2, weight, LAYOUT_NT, iters, mode,
                bias=bias if (bias is not None and bias.numel() > 0) else None,
                act=act, residual=r2)
-    shape[-1] = weight.shape[0]
+    shape[-1] = weight.shape[0] // 2 if act == ACT_SWIGLU else weight.shape[0]
     out = out.reshape(shape)
     return out if dt == torch.float32 else out.to(dt)
 

@@ -297,7 +297,22 @@ class RACGatedFFN(nn.Module):
     def forward(self, x):
         return self.down(self.gate(x) * self.up(x))
 
+    def _gate_up(self) -> torch.Tensor:
+        """gate and up weights row-interleaved ([2F, d]) for the one-GEMM SwiGLU;
+        derived state, rebuilt whenever either weight's storage or version changes."""
+        key = tuple((w.data_ptr(), w._version, tuple(w.shape), w.device)
+                    for w in (self.gate.weight, self.up.weight))
+        if getattr(self, "_gu_key", None) != key:
+            with torch.no_grad():
+                self._gu = torch.stack([self.gate.weight, self.up.weight], 1).reshape(
+                    -1, self.gate.weight.shape[1]).float().contiguous()
+            self._gu_key = key
+        return self._gu
+
     def forward_residual(self, x, residual):
+        if self.gate.bias is None and self.up.bias is None:
+            h = ext.linear_forward(x, self._gate_up(), None, act=ext.ACT_SWIGLU, **_kw())
+            return self.down.forward_residual(h, residual)
         g = ext.linear_forward(x, self.gate.weight, self.gate.bias, act=ACT_SILU, **_kw())
         u = ext.linear_forward(x, self.up.weight, self.up.bias, **_kw())
         return self.down.forward_residual(g.mul_(u), residual)

@@ -9,6 +9,8 @@
   qkv and the FFN up-projections split by output rows (whole heads / ff
   slices per rank), out_proj and the down-projection split by input columns,
   one NCCL all-reduce (sum, fp32) after each of the two row-split GEMMs.
+  The gated FFN's gate and up shards run as one GEMM over row-interleaved
+  weights whose epilogue writes silu(gate) * up.
   Rank 0 adds the residual in its GEMM epilogue so the all-reduce yields
   x + sum of partials directly.
 """
@@ -68,9 +70,10 @@ class TPLlamaBlock(nn.Module):
         if self.gated:
             ff = f.up.out_features
             f0, f1 = ff * rank // world, ff * (rank + 1) // world
-            self.w_gate = _linear_from(f.gate.weight.data[f0:f1])
-            self.w_up = _linear_from(f.up.weight.data[f0:f1])
             self.w_down = _linear_from(f.down.weight.data[:, f0:f1])
+            # gate and up rows interleaved: one GEMM with the SwiGLU epilogue
+            self.w_gu = _linear_from(interleave_rows(f.gate.weight.data[f0:f1],
+                                                     f.up.weight.data[f0:f1]))
         else:
             ff = f.fc1.out_features
             f0, f1 = ff * rank // world, ff * (rank + 1) // world
@@ -85,7 +88,8 @@ class TPLlamaBlock(nn.Module):
         p = {"norm1": g(self.norm1.weight), "qkv": g(self.attn.qkv.weight),
              "out": g(self.attn.out_proj.weight), "norm2": g(self.norm2.weight)}
         if self.gated:
-            p.update(gate=g(self.w_gate.weight), up=g(self.w_up.weight), down=g(self.w_down.weight))
+            gu = g(self.w_gu.weight)
+            p.update(gate=gu[0::2].contiguous(), up=gu[1::2].contiguous(), down=g(self.w_down.weight))
         else:
             p.update(fc1=g(self.w_fc1.weight), fc2=g(self.w_fc2.weight))
         return p
@@ -104,9 +108,7 @@ class TPLlamaBlock(nn.Module):
         n2 = self.norm2(h)
         res = h if self.rank == 0 else None
         if self.gated:
-            g = _apply(n2, self.w_gate, act=ext.ACT_SILU)
-            u = _apply(n2, self.w_up)
-            y = _apply(g.mul_(u), self.w_down, residual=res)
+            y = _apply(_apply(n2, self.w_gu, act=ext.ACT_SWIGLU), self.w_down, residual=res)
         else:
             t = _apply(n2, self.w_fc1, act=self.act_id)
             y = _apply(t, self.w_fc2, residual=res)
@@ -154,8 +156,13 @@ def _apply(x: torch.Tensor, lin: _ShardLinear, act: int = ext.ACT_NONE,
     r2 = residual.reshape(-1, out_f) if residual is not None else None
     out = ext.gemm(x.reshape(-1, in_f), lin.weight_t(), ext.LAYOUT_NN, kw["iters"], kw["mode"],
                    act=act, residual=r2)
-    shape[-1] = out_f
+    shape[-1] = out.shape[-1]
     return out.reshape(shape)
+
+
+def interleave_rows(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[2F, d] with gate row c at 2c and up row c at 2c+1 (the SwiGLU GEMM's B)."""
+    return torch.stack([gate, up], dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
 
 
 def _linear_from(w: torch.Tensor) -> nn.Module:

@@ -5,8 +5,8 @@ with the OpenMP restatement (which finishes these in seconds):
   iterations: bit-exact;
 * rac_rope_apply on Q [8, 32, 4096, 128]: bit-exact;
 * rac_softmax_batch on [32768, 4096] ~N(0, 9): max relative error <= 1e-4;
-* rac_rmsnorm / rac_layernorm on [16384, 4096]: the reduction bars of the
-  reduced-size tests.
+* rac_rmsnorm on [16384, 4096]: max relative error <= 1e-4; rac_layernorm
+  on the same: bit-exact (it keeps lib/c's sequential accumulation order).
 
 Each call runs through the stream-ordered C ABI on device tensors, as the
 benchmark does.  Sizes and distributions follow the benchmark configs.
@@ -67,11 +67,7 @@ def test_norms_full(cuda, orc):
     got = ext.rmsnorm(xd, _t(g, cuda), 1e-6).cpu().numpy()
     assert O.max_rel_err(got, orc.rmsnorm(x, g, 1e-6)) <= 1e-4
     got = ext.layernorm(xd, _t(g, cuda), _t(b, cuda), 1e-6).cpu().numpy()
-    rows = slice(0, 16384, 61)                 # float64 exact result on a row sample
-    xs = x[rows].astype(np.float64)
-    m = xs.mean(1, keepdims=True)
-    exact = g * (xs - m) / np.sqrt(((xs - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
     want = orc.layernorm(x, g, b, 1e-6)
-    assert O.reduction_ok(got[rows], want[rows], exact)
-    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
-    assert float(np.abs(got - want).max()) / rms <= 1e-5           # normwise, every row
+    err = O.max_rel_err(got, want)
+    print(f"layernorm [16384, 4096] max-rel vs lib/c order: {err:.3e}")
+    assert np.array_equal(got, want)          # lib/c's sequential mean / variance, bit for bit

@@ -313,5 +313,57 @@ def test_gemm_bitexact_vs_reference_hip_code(cuda, mode, iters):
 
 def _same_bits(x, y):
     """Bit-equal, except that any NaN matches any NaN (the GPU's canonical NaN
-    and the host's differ in sign and payload)."""
-    return bool(((x.view(np.uint32) == y.view(np.uint32)) | (np.isnan(x) & np.isnan(y))).all())
+    and the host's differ in sign and payload) and +0 matches -0: where the
+    exact value of a fused multiply-add is a negative number too small to
+    represent (e.g. 1e-40 * -1e-40 + 0), IEEE rounding gives -0.0 and the host
+    returns -0.0, while the GPU's FFMA returns +0.0 -- equal values, different
+    sign bits."""
+    zero = (x == 0) & (y == 0)
+    return bool(((x.view(np.uint32) == y.view(np.uint32)) | (np.isnan(x) & np.isnan(y)) | zero).all())
+
+
+@pytest.mark.parametrize("mode,iters", [(0, 24), (1, 16), (1, 8), (2, 8)])
+@pytest.mark.parametrize("M,variant", [(96, 0), (16, 0), (70, 13)])
+def test_swiglu_epilogue_equals_two_gemms(cuda, mode, iters, M, variant):
+    """RAC_ACT_SWIGLU over row-interleaved [gate; up] weights gives the bits of a
+    SiLU GEMM on the gate rows times a plain GEMM on the up rows (NT and NN on
+    the transposed weights; split-K when M is small or the variant forces it),
+    with and without a bias."""
+    F_, K = 100, 1300
+    rng = np.random.default_rng(M + iters)
+    x = _t(rng.uniform(-1, 1, (M, K)).astype(np.float32), cuda)
+    wg = _t((rng.standard_normal((F_, K)) * 0.05).astype(np.float32), cuda)
+    wu = _t((rng.standard_normal((F_, K)) * 0.05).astype(np.float32), cuda)
+    bg = _t(rng.standard_normal(F_).astype(np.float32), cuda)
+    bu = _t(rng.standard_normal(F_).astype(np.float32), cuda)
+    wgu = torch.stack([wg, wu], 1).reshape(2 * F_, K).contiguous()
+    bgu = torch.stack([bg, bu], 1).reshape(2 * F_).contiguous()
+    for bias in (False, True):
+        g = ext.gemm(x, wg, LAYOUT_NT, iters, mode, act=ext.ACT_SILU, bias=bg if bias else None,
+                     variant=variant)
+        u = ext.gemm(x, wu, LAYOUT_NT, iters, mode, bias=bu if bias else None, variant=variant)
+        want = g * u
+        got = ext.gemm(x, wgu, LAYOUT_NT, iters, mode, act=ext.ACT_SWIGLU,
+                       bias=bgu if bias else None, variant=variant)
+        assert got.shape == (M, F_) and torch.equal(got, want), bias
+        got_nn = ext.gemm(x, wgu.t().contiguous(), LAYOUT_NN, iters, mode, act=ext.ACT_SWIGLU,
+                          bias=bgu if bias else None, variant=variant)
+        assert torch.equal(got_nn, want), bias
+
+
+@pytest.mark.parametrize("variant", [0, 0x400, 13, 0x2000])
+@pytest.mark.parametrize("layout", ["nn", "nt", "tn"])
+@pytest.mark.parametrize("shape", [(200, 328, 256), (64, 128, 8), (132, 260, 36)])
+def test_fast_kernels_bitexact(cuda, orc, variant, layout, shape):
+    """FAST mode: the TMA-staged FFMA2 kernel (NN/TN; 64x128 tiles, or 128x128
+    with bit 0x2000), the general one-FFMA kernel (bit 0x400, and NT) and split-K
+    (13): the restatement's bits (each FFMA2 half is one fused multiply-add,
+    sequential over k)."""
+    M, N, K = shape
+    A, B = _operands(M, N, K, layout, M + N + K + variant)
+    got = ext.gemm(_t(A, cuda), _t(B, cuda), LAY[layout], 24, 0, variant=variant).cpu().numpy()
+    want = orc.gemm(A, B, layout, 0, 24)
+    if variant == 13:                                 # split-K: a different summation order
+        assert _normwise(got, want) <= NORM_TOL
+    else:
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))

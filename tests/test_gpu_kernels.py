@@ -169,7 +169,8 @@ def test_softmax_golden_host_abi(cuda, golden):
     assert O.max_rel_err(out, golden["softmax_out"]) <= 1e-4
 
 
-@pytest.mark.parametrize("shape", [(5, 4096), (31, 4096), (7, 1003), (4, 16384), (2, 4)])
+@pytest.mark.parametrize("shape", [(5, 4096), (31, 4096), (7, 1003), (4, 16384), (2, 4),
+                                   (33, 4100), (70, 36), (65, 128)])
 def test_norms(cuda, orc, shape):
     rng = np.random.default_rng(shape[1] + 1)
     x = rng.standard_normal(shape).astype(np.float32)
@@ -178,10 +179,7 @@ def test_norms(cuda, orc, shape):
     got = ext.rmsnorm(_t(x, cuda), _t(g, cuda), 1e-6).cpu().numpy()
     assert O.max_rel_err(got, orc.rmsnorm(x, g, 1e-6)) <= 1e-4
     got = ext.layernorm(_t(x, cuda), _t(g, cuda), _t(b, cuda), 1e-6).cpu().numpy()
-    xd = x.astype(np.float64)
-    m = xd.mean(1, keepdims=True)
-    exact = g * (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
-    assert O.reduction_ok(got, orc.layernorm(x, g, b, 1e-6), exact)
+    assert np.array_equal(got, orc.layernorm(x, g, b, 1e-6))          # lib/c's sequential order
     got = ext.rmsnorm(_t(x, cuda), None, 1e-6).cpu().numpy()
     assert O.max_rel_err(got, orc.rmsnorm(x, None, 1e-6)) <= 1e-4
 
@@ -195,10 +193,24 @@ def test_norms_golden_host_abi(cuda, golden):
     assert O.max_rel_err(y, golden["rms_out"]) <= 1e-4
     L.rac_layernorm(_p(x), _p(y), _p(g), _p(b), ctypes.c_float(1e-6), x.shape[0], x.shape[1])
     _lib.check()
-    xd = x.astype(np.float64)
-    m = xd.mean(1, keepdims=True)
-    exact = g * (xd - m) / np.sqrt(((xd - m) ** 2).mean(1, keepdims=True) + 1e-6) + b
-    assert O.reduction_ok(y, golden["ln_out"], exact)
+    assert np.array_equal(y, golden["ln_out"])          # bit-identical to the reference lib/c
+
+
+@pytest.mark.parametrize("shape", [(40, 64), (3, 4097)])
+def test_layernorm_edges(cuda, orc, shape):
+    """No gamma / beta, a constant row with eps = 0 (variance 0: lib/c's rac_rsqrt
+    gives 0, so the row maps to beta), unaligned rows (the one-thread-per-row
+    path), all bit-exact to the restatement."""
+    rng = np.random.default_rng(shape[1])
+    x = rng.standard_normal(shape).astype(np.float32)
+    x[1] = 0.75
+    got = ext.layernorm(_t(x, cuda), None, None, 0.0).cpu().numpy()
+    assert np.array_equal(got, orc.layernorm(x, None, None, 0.0))
+    big = torch.zeros(shape[0] * shape[1] + 1, device=cuda)
+    xs = big[1:].view(shape)                                # 4-byte aligned, not 16
+    xs.copy_(_t(x, cuda))
+    got = ext.layernorm(xs, None, None, 1e-5).cpu().numpy()
+    assert np.array_equal(got, orc.layernorm(x, None, None, 1e-5))
 
 
 @pytest.mark.parametrize("it", [4, 7, 8, 16, 24])

@@ -38,7 +38,9 @@ def test_tp_shards_rebuild_full_weights(gated, world):
     o = torch.cat([s.attn.out_proj.weight for s in shards], 1)
     assert torch.equal(o, full.attn.out_proj.weight)
     if gated:
-        assert torch.equal(torch.cat([s.w_up.weight for s in shards], 0), full.ffn.up.weight)
+        gu = [s.w_gu.weight for s in shards]          # gate row c at 2c, up row c at 2c+1
+        assert torch.equal(torch.cat([w[0::2] for w in gu], 0), full.ffn.gate.weight)
+        assert torch.equal(torch.cat([w[1::2] for w in gu], 0), full.ffn.up.weight)
         assert torch.equal(torch.cat([s.w_down.weight for s in shards], 1), full.ffn.down.weight)
     else:
         assert torch.equal(torch.cat([s.w_fc1.weight for s in shards], 0), full.ffn.fc1.weight)
