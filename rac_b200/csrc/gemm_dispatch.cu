@@ -69,8 +69,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-static bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
-                      long long ld, uint32_t box_inner, uint32_t box_outer) {
+bool encode_tensor_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                      long long ld, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     if ((reinterpret_cast<uintptr_t>(base) & 15u) || ((ld * 4) & 15)) return false;
@@ -79,8 +79,14 @@ static bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint6
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool encode_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                      long long ld, uint32_t box_inner, uint32_t box_outer) {
+    return encode_tensor_2d(map, base, inner, outer, ld, box_inner, box_outer, false);
 }
 
 bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK) {

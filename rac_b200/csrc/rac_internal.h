@@ -59,6 +59,10 @@ struct GemmParams {
 // Returns false when the operands do not meet the TMA rules (16-byte aligned
 // bases and leading dimensions) or the driver entry point is unavailable.
 bool make_tensor_maps(GemmParams& p, int layout, int BM, int BN, int BK);
+// A 2-D fp32 tensor map (inner dim contiguous, rows ld floats apart) with a
+// box_inner x box_outer box; swizzle128 selects the 128-byte swizzle.
+bool encode_tensor_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                      long long ld, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 
 // launch_gemm without the split-K decision: launches the tile kernel for p
 // as given (p.ws == nullptr: whole K per CTA).

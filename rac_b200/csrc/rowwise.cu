@@ -18,7 +18,7 @@
 // reference at [16384, 4096]).  So LayerNorm reproduces lib/c's sequential
 // mean and variance chains exactly (k_layernorm_seq below) and is
 // bit-identical to it.
-#include <cstdlib>
+#include <atomic>
 
 #include "rac_device.cuh"
 #include "rac_internal.h"
@@ -193,172 +193,278 @@ static int launch_rows(const float* x, float* y, const float* g, float eps, long
 // and var = fmaf(z_{d-1}, z_{d-1}, ... fmaf(z0, z0, 0))/d with z = x - mean:
 // two chains of d dependent roundings.  A chain cannot be split without
 // changing its bits, so the kernel runs one chain per row, one row per lane,
-// and gets its parallelism from many rows.
+// and gets its parallelism from many rows.  Each row is therefore read three
+// times (mean chain, variance chain, output) and written once.
 //
-// A warp owns a group of 32 rows and streams it three times through a ring
-// of kLnStages shared-memory chunks of 32 rows x 32 columns (cp.async,
-// 16-byte pieces, coalesced in 128-byte row segments; row stride 36 floats,
-// so each lane's 128-bit reads and writes of its own row are bank-conflict
-// free): pass 0 runs the mean chains, pass 1 the variance chains, pass 2
-// computes y = fmaf(gamma, (x - mean) * inv, beta) in the lane's row, writes
-// it back into the chunk and stores the chunk with coalesced 128-bit stores.
-// The loads form one continuous stream across passes and groups, kLnStages
-// - 1 chunks ahead.  The kernel is persistent with few groups per SM in
-// flight, so the second and third reads of a group come from L2: a group is
-// 512 KB and is re-read within microseconds.  gamma and beta are staged in
-// shared memory once per CTA when d <= kLnMaxD.
+// One persistent CTA per SM: kLnChains chain warps, each owning a group of 32
+// rows (one per lane) at a time, and the remaining warps writing outputs.
+//  * A chain warp streams its group twice through its own ring of kLnStages
+//    shared-memory chunks of 32 rows x kLnCW columns.  Lane 0 fills a stage
+//    with kLnCW / 32 TMA copies (cp.async.bulk.tensor.2d, a 32 x 32 box, the
+//    128-byte swizzle, no multicast) that complete on the stage's mbarrier;
+//    the swizzle puts lane r's 16-byte piece q of its row at slot q ^ (r & 7),
+//    so the lanes' 128-bit reads of their own rows are bank-conflict free.
+//    The reads run kLnNB float4 ahead of the chain (software pipelining),
+//    so a chain step costs ~4.5 cycles, the dependent FADD / FFMA latency.
+//    Pass 0 runs the mean chains, pass 1 the variance chains; the copies form
+//    one continuous stream across passes and groups, kLnStages - 1 chunks
+//    ahead.
+//  * Meanwhile the output warps write y = fmaf(gamma, (x - mean) * inv, beta)
+//    for the previous round's groups, row by row with coalesced 128-bit
+//    accesses, kLnOut loads in flight per lane (gamma / beta staged in shared
+//    memory).
+//  * One __syncthreads per round hands the groups' mean / inv from the chain
+//    warps to the output warps (double-buffered).
+// Measured at [16384, 4096]: 0.188 ms, 1.01 GB of DRAM traffic (three reads
+// and one write: a row's reads are too far apart for L2 to keep it), i.e.
+// 5.4 TB/s, near that traffic's HBM floor of 0.155 ms; the tree-ordered
+// one-read kernel this replaced ran in 0.090 ms but was 4.3e-4 (max-rel) from
+// the reference.  Every mbarrier wait is bounded: a copy that never lands
+// sets bit 2 of the device error word, and the warp stops issuing and drains
+// (bounded) instead of hanging.
 constexpr int kLnRows = 32;
-constexpr int kLnChunk = 32;
-constexpr int kLnLd = 36;
-constexpr int kLnStages = 12;
-constexpr int kLnMaxD = 4096;
-constexpr int kLnCtasPerSm = 2;
-constexpr int kLnRing = kLnStages * kLnRows * kLnLd;          // floats
+constexpr int kLnThreads = 256;                                // chain warps first, then output
+constexpr int kLnMaxGB = 4096;                                 // gamma / beta staged up to this d
+constexpr int kLnOut = 16;                                     // output loads in flight per lane
+constexpr int kLnNB = 8;                                       // float4 per chain batch
+constexpr uint32_t kLnWaitLimit = 1u << 22;
 
-__device__ __forceinline__ void ln_cp16(float* dst, const float* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                 :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
+__device__ __forceinline__ uint32_t ln_smem(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void ln_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void ln_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+__device__ __forceinline__ bool ln_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(ln_smem(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
 
 // rac_rsqrt of lib/c/rac_cpu.c:330-335.
 __device__ __forceinline__ float ln_rsqrt(float v) {
     return v <= 0.0f ? 0.0f : __fdiv_rn(1.0f, __fsqrt_rn(v));
 }
 
-__global__ void __launch_bounds__(32) k_layernorm_seq(const float* __restrict__ x,
-                                                      float* __restrict__ y,
-                                                      const float* __restrict__ gamma,
-                                                      const float* __restrict__ beta,
-                                                      float eps, int d, long long rows) {
-    extern __shared__ __align__(16) float smem[];
-    float* ring = smem;
-    const bool staged = d <= kLnMaxD;
-    float* sg = smem + kLnRing;                 // gamma, beta (staged: d floats each)
-    float* sb = sg + kLnMaxD;
-    const int lane = threadIdx.x;
+// kLnCW: chunk width (floats, a multiple of 32); kLnStages: ring depth.
+// tmx: x as a [rows, d] tensor map with a 32 x 32 box and the 128-byte swizzle.
+template <int kLnCW, int kLnStages, int kLnChains>
+__global__ void __launch_bounds__(kLnThreads) k_layernorm_seq(const __grid_constant__ CUtensorMap tmx,
+                                                              const float* __restrict__ x,
+                                                              float* __restrict__ y,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta,
+                                                              float eps, int d, long long rows,
+                                                              unsigned int* err) {
+    static_assert(kLnCW % 32 == 0, "chunks are whole 32-column slabs");
+    constexpr int kStage = kLnRows * kLnCW;                    // floats per stage
+    extern __shared__ __align__(1024) float lnsm[];
+    // the swizzled TMA destination wants 1024-byte alignment
+    float* ring0 = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(lnsm) + 1023) & ~uintptr_t(1023));
+    // gamma and beta staged after the rings when d <= kLnMaxGB (1 where absent)
+    const bool staged = d <= kLnMaxGB;
+    float* sg = ring0 + kLnChains * kLnStages * kStage;
+    float* sb = sg + kLnMaxGB;
+    __shared__ float s_mean[2][kLnChains * kLnRows], s_inv[2][kLnChains * kLnRows];
+    __shared__ __align__(8) uint64_t fullb[kLnChains][kLnStages];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp < kLnChains ? warp : 0;    // this chain warp's ring and barriers
+    float* ring = ring0 + cw * kLnStages * kStage;
+    uint64_t* full = fullb[cw];
     const long long groups = (rows + kLnRows - 1) / kLnRows;
-    const int nch = (d + kLnChunk - 1) / kLnChunk;
+    const long long my_groups = groups > blockIdx.x ? (groups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nch = (d + kLnCW - 1) / kLnCW;
     const float fd = (float)d;
+
+    // chain warp: producer (bulk copies) and consumer (chains) positions
+    long long pg = blockIdx.x + (long long)cw * gridDim.x, pgi = cw;
+    int ppass = 0, pc = 0, pst = 0;
+    int outstanding = 0;                        // chunks issued and not yet waited for
+    bool bad = false;                           // a wait ran out: stop issuing, drain, report
+    auto issue = [&]() {
+        if (pgi < my_groups && !bad) {
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                             :: "r"(ln_smem(&full[pst])), "r"((uint32_t)(kStage * 4)) : "memory");
+                float* dst = ring + pst * kStage;
+#pragma unroll
+                for (int sl = 0; sl < kLnCW / 32; ++sl)   // one 32 x 32 box per slab
+                    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                                 " [%0], [%1, {%2, %3}], [%4];"
+                                 :: "r"(ln_smem(dst + sl * 1024)), "l"(reinterpret_cast<uint64_t>(&tmx)),
+                                    "r"(pc * kLnCW + 32 * sl), "r"((int)(pg * kLnRows)),
+                                    "r"(ln_smem(&full[pst])) : "memory");
+            }
+            ++outstanding;
+            if (++pc == nch) {
+                pc = 0;
+                if (++ppass == 2) { ppass = 0; pg += (long long)kLnChains * gridDim.x; pgi += kLnChains; }
+            }
+        }
+        if (++pst == kLnStages) pst = 0;
+    };
+    if (warp < kLnChains) {
+        if (lane == 0) {
+            for (int st = 0; st < kLnStages; ++st)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(ln_smem(&full[st])));
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncwarp();
+        if (pgi < my_groups) {
+#pragma unroll 1
+            for (int t = 0; t < kLnStages - 1; ++t) issue();
+        }
+    }
     if (staged) {
-        for (int i = lane; i < d; i += 32) {
+        for (int i = threadIdx.x; i < d; i += kLnThreads) {
             sg[i] = gamma ? gamma[i] : 1.0f;
             sb[i] = beta ? beta[i] : 0.0f;
         }
     }
-    // This CTA's chunk stream, group by group: pass 0, 1, 2 over chunks 0..nch-1.
-    // Producer and consumer each walk it with counters (no divisions).
-    const long long my_groups = groups > blockIdx.x ? (groups - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    long long pg = blockIdx.x;                  // producer: group, pass, chunk, stage
-    int ppass = 0, pc = 0, pst = 0;
-    long long issued_groups = 0;
-    auto issue = [&]() {
-        if (issued_groups < my_groups) {
-            const long long r0 = pg * kLnRows;
-            const int nr = (int)(rows - r0 < kLnRows ? rows - r0 : kLnRows);
-            float* st = ring + pst * (kLnRows * kLnLd);
-#pragma unroll
-            for (int i = 0; i < kLnRows * kLnChunk / 4 / 32; ++i) {
-                const int idx = lane + 32 * i, rr = idx >> 3, q = idx & 7;
-                const int col = pc * kLnChunk + 4 * q;
-                if (rr < nr && col < d)
-                    ln_cp16(st + rr * kLnLd + 4 * q, x + (r0 + rr) * (long long)d + col);
-            }
-            if (++pc == nch) {
-                pc = 0;
-                if (++ppass == 3) { ppass = 0; pg += gridDim.x; ++issued_groups; }
-            }
-        }
-        if (++pst == kLnStages) pst = 0;
-        ln_commit();                            // one group of copies per step, empty or not
-    };
+    __syncthreads();
+    int cst = 0;
+    uint32_t cpar = 0;                          // parity of the current use of the ring
 #pragma unroll 1
-    for (int t = 0; t < kLnStages - 1; ++t) issue();
-    __syncwarp();                               // gamma / beta staged
-    float acc = 0.0f, mean = 0.0f, inv = 0.0f;
-    long long cg = blockIdx.x;                  // consumer: group, pass, chunk, stage
-    int pass = 0, c = 0, cst = 0;
+    const long long rounds = (my_groups + kLnChains - 1) / kLnChains;
+    for (long long k = 0; k <= rounds; ++k) {
+        const int slot = (int)(k & 1);
+        if (warp < kLnChains && k * kLnChains + warp < my_groups) {
+            // ── chains of group k: pass 0 (mean), pass 1 (variance) ──
+            float acc = 0.0f, mean = 0.0f;
 #pragma unroll 1
-    for (long long done = 0; done < my_groups;) {
-        issue();
-        ln_wait<kLnStages - 1>();               // this lane's pieces of the chunk landed
-        __syncwarp();                           // ... and every other lane's
-        if (c == 0) {
-            if (pass == 0) acc = 0.0f;
-            if (pass == 1) { mean = __fdiv_rn(acc, fd); acc = 0.0f; }   // mean /= (float)d
-            if (pass == 2) inv = ln_rsqrt(__fadd_rn(__fdiv_rn(acc, fd), eps));
-        }
-        float* chunk = ring + cst * (kLnRows * kLnLd);
-        float* rowp = chunk + lane * kLnLd;
-        const int w = min(kLnChunk, d - c * kLnChunk);
-        if (pass < 2) {
-            if (w == kLnChunk) {
-                float v[kLnChunk];
+            for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll 1
+                for (int c = 0; c < nch; ++c) {
+                    issue();
+                    if (!bad) {
+                        bool timed_out = false;
+                        uint32_t polls = 0;
+                        while (!ln_try_wait(&full[cst], cpar)) {
+                            if (++polls >= kLnWaitLimit) { timed_out = true; break; }
+                        }
+                        if (__any_sync(0xffffffffu, timed_out)) {
+                            // Report, then wait (bounded) for every copy still in
+                            // flight, in issue order, so none lands after the CTA
+                            // exits; from here on nothing is issued or awaited.
+                            if (lane == 0 && err) atomicOr(err, 4u);
+                            int s2 = cst;
+                            uint32_t p2 = cpar;
+                            for (int i = 0; i < outstanding; ++i) {
+                                uint32_t n = 0;
+                                while (!ln_try_wait(&full[s2], p2) && ++n < kLnWaitLimit) {}
+                                if (++s2 == kLnStages) { s2 = 0; p2 ^= 1u; }
+                            }
+                            outstanding = 0;
+                            bad = true;
+                        } else {
+                            --outstanding;
+                        }
+                    }
+                    // lane's row: slab sl holds columns 32 sl .. 32 sl + 31 at
+                    // rowp + sl * 1024; its 16-byte piece q sits at slot q ^ (lane & 7)
+                    const float* rowp = ring + cst * kStage + lane * 32;
+                    const int sw = lane & 7;
+                    const int w = min(kLnCW, d - c * kLnCW);
+                    if (w == kLnCW) {
+                        // software-pipelined: the next kLnNB float4 of the row are
+                        // read from shared memory while the chain runs on these
+                        auto rd = [&](int u) {          // float4 u of the lane's row
+                            return *reinterpret_cast<const float4*>(rowp + (u >> 3) * 1024 + (((u & 7) ^ sw) << 2));
+                        };
+                        float4 cur[kLnNB], nxt[kLnNB];
 #pragma unroll
-                for (int q = 0; q < kLnChunk / 4; ++q) {
-                    const float4 f = *reinterpret_cast<const float4*>(rowp + 4 * q);
-                    v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+                        for (int u = 0; u < kLnNB; ++u) cur[u] = rd(u);
+                        if (pass == 0) {
+#pragma unroll
+                            for (int bq = 0; bq < kLnCW / 4; bq += kLnNB) {
+                                if (bq + kLnNB < kLnCW / 4) {
+#pragma unroll
+                                    for (int u = 0; u < kLnNB; ++u) nxt[u] = rd(bq + kLnNB + u);
+                                }
+#pragma unroll
+                                for (int u = 0; u < kLnNB; ++u) {
+                                    acc = __fadd_rn(acc, cur[u].x); acc = __fadd_rn(acc, cur[u].y);
+                                    acc = __fadd_rn(acc, cur[u].z); acc = __fadd_rn(acc, cur[u].w);
+                                }
+#pragma unroll
+                                for (int u = 0; u < kLnNB; ++u) cur[u] = nxt[u];
+                            }
+                        } else {
+#pragma unroll
+                            for (int bq = 0; bq < kLnCW / 4; bq += kLnNB) {
+                                if (bq + kLnNB < kLnCW / 4) {
+#pragma unroll
+                                    for (int u = 0; u < kLnNB; ++u) nxt[u] = rd(bq + kLnNB + u);
+                                }
+#pragma unroll
+                                for (int u = 0; u < kLnNB; ++u) {
+                                    float z;
+                                    z = __fsub_rn(cur[u].x, mean); acc = __fmaf_rn(z, z, acc);
+                                    z = __fsub_rn(cur[u].y, mean); acc = __fmaf_rn(z, z, acc);
+                                    z = __fsub_rn(cur[u].z, mean); acc = __fmaf_rn(z, z, acc);
+                                    z = __fsub_rn(cur[u].w, mean); acc = __fmaf_rn(z, z, acc);
+                                }
+#pragma unroll
+                                for (int u = 0; u < kLnNB; ++u) cur[u] = nxt[u];
+                            }
+                        }
+                    } else {
+#pragma unroll 1
+                        for (int q = 0; q < w; ++q) {
+                            const float vq = rowp[(q >> 5) * 1024 + ((((q >> 2) & 7) ^ sw) << 2) + (q & 3)];
+                            if (pass == 0) acc = __fadd_rn(acc, vq);
+                            else { const float z = __fsub_rn(vq, mean); acc = __fmaf_rn(z, z, acc); }
+                        }
+                    }
+                    __syncwarp();               // every lane is done with the stage
+                    if (++cst == kLnStages) { cst = 0; cpar ^= 1u; }
                 }
-                if (pass == 0) {
+                if (pass == 0) { mean = __fdiv_rn(acc, fd); acc = 0.0f; }   // mean /= (float)d
+            }
+            s_mean[slot][cw * kLnRows + lane] = mean;
+            s_inv[slot][cw * kLnRows + lane] = ln_rsqrt(__fadd_rn(__fdiv_rn(acc, fd), eps));
+        } else if (warp >= kLnChains && k >= 1) {
+            // ── output of the previous round's groups ──
+            const int ps = slot ^ 1;
+            const int nq = d >> 2;
+            const float4* g4 = reinterpret_cast<const float4*>(staged ? sg : gamma);
+            const float4* b4 = reinterpret_cast<const float4*>(staged ? sb : beta);
+            for (int ra = warp - kLnChains; ra < kLnChains * kLnRows; ra += kLnThreads / 32 - kLnChains) {
+                const long long j = (k - 1) * kLnChains + ra / kLnRows;      // local group
+                if (j >= my_groups) break;
+                const int rr = ra % kLnRows;
+                const long long r0 = ((long long)blockIdx.x + j * gridDim.x) * kLnRows;
+                if (r0 + rr >= rows) continue;
+                const float m = s_mean[ps][ra], inv = s_inv[ps][ra];
+                const float4* xr = reinterpret_cast<const float4*>(x + (r0 + rr) * (long long)d);
+                float4* yr = reinterpret_cast<float4*>(y + (r0 + rr) * (long long)d);
+                // kLnOut loads of a lane in flight at once, then the stores
+                for (int q0 = lane; q0 < nq; q0 += 32 * kLnOut) {
+                    float4 v[kLnOut];
 #pragma unroll
-                    for (int k = 0; k < kLnChunk; ++k) acc = __fadd_rn(acc, v[k]);
-                } else {
+                    for (int u = 0; u < kLnOut; ++u) {
+                        const int q = q0 + 32 * u;
+                        v[u] = q < nq ? __ldcg(xr + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
 #pragma unroll
-                    for (int k = 0; k < kLnChunk; ++k) {
-                        const float z = __fsub_rn(v[k], mean);
-                        acc = __fmaf_rn(z, z, acc);
+                    for (int u = 0; u < kLnOut; ++u) {
+                        const int q = q0 + 32 * u;
+                        if (q < nq) {
+                            const float4 g = g4 ? g4[q] : make_float4(1.f, 1.f, 1.f, 1.f);
+                            const float4 b = b4 ? b4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+                            __stcs(yr + q, make_float4(
+                                __fmaf_rn(g.x, __fmul_rn(__fsub_rn(v[u].x, m), inv), b.x),
+                                __fmaf_rn(g.y, __fmul_rn(__fsub_rn(v[u].y, m), inv), b.y),
+                                __fmaf_rn(g.z, __fmul_rn(__fsub_rn(v[u].z, m), inv), b.z),
+                                __fmaf_rn(g.w, __fmul_rn(__fsub_rn(v[u].w, m), inv), b.w)));
+                        }
                     }
                 }
-            } else {
-#pragma unroll 1
-                for (int k = 0; k < w; ++k) {
-                    const float vk = rowp[k];
-                    if (pass == 0) acc = __fadd_rn(acc, vk);
-                    else { const float z = __fsub_rn(vk, mean); acc = __fmaf_rn(z, z, acc); }
-                }
-            }
-        } else {
-            const int c0 = c * kLnChunk;
-            // y for this lane's row, written back over x in the chunk
-#pragma unroll 2
-            for (int q = 0; q < w / 4; ++q) {
-                const float4 f = *reinterpret_cast<const float4*>(rowp + 4 * q);
-                float4 g4, b4;
-                if (staged) {
-                    g4 = *reinterpret_cast<const float4*>(sg + c0 + 4 * q);
-                    b4 = *reinterpret_cast<const float4*>(sb + c0 + 4 * q);
-                } else {
-                    g4 = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c0) + q) : make_float4(1.f, 1.f, 1.f, 1.f);
-                    b4 = beta ? __ldg(reinterpret_cast<const float4*>(beta + c0) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-                *reinterpret_cast<float4*>(rowp + 4 * q) =
-                    make_float4(__fmaf_rn(g4.x, __fmul_rn(__fsub_rn(f.x, mean), inv), b4.x),
-                                __fmaf_rn(g4.y, __fmul_rn(__fsub_rn(f.y, mean), inv), b4.y),
-                                __fmaf_rn(g4.z, __fmul_rn(__fsub_rn(f.z, mean), inv), b4.z),
-                                __fmaf_rn(g4.w, __fmul_rn(__fsub_rn(f.w, mean), inv), b4.w));
-            }
-            __syncwarp();                       // the chunk now holds y; store it coalesced
-            const long long r0 = cg * kLnRows;
-            const int nr = (int)(rows - r0 < kLnRows ? rows - r0 : kLnRows);
-#pragma unroll
-            for (int i = 0; i < kLnRows * kLnChunk / 4 / 32; ++i) {
-                const int idx = lane + 32 * i, rr = idx >> 3, q = idx & 7;
-                const int col = c0 + 4 * q;
-                if (rr < nr && col < d)
-                    __stcs(reinterpret_cast<float4*>(y + (r0 + rr) * (long long)d + col),
-                           *reinterpret_cast<const float4*>(chunk + rr * kLnLd + 4 * q));
             }
         }
-        __syncwarp();                           // the stage is re-filled next iteration
-        if (++cst == kLnStages) cst = 0;
-        if (++c == nch) {
-            c = 0;
-            if (++pass == 3) { pass = 0; cg += gridDim.x; ++done; }
-        }
+        __syncthreads();                        // group k's stats -> output warps; slot reuse
     }
-    ln_wait<0>();
 }
 
 // Any d and alignment: one thread per row, the same chains straight from
@@ -390,40 +496,48 @@ int rmsnorm_rows(const float* x, float* y, const float* gamma, float eps, long l
                  cudaStream_t s) {
     return launch_rows<kRowRms>(x, y, gamma, eps, rows, d, s);
 }
+// One persistent CTA per SM (the grid never exceeds the number of groups).
+template <int CW, int ST, int CH>
+static int launch_ln(const float* x, float* y, const float* gamma, const float* beta, float eps,
+                     int d, long long rows, int dev, cudaStream_t s) {
+    const int smem = (CH * ST * kLnRows * CW + 2 * kLnMaxGB) * (int)sizeof(float) + 1024;
+    CUtensorMap tmx;
+    if (!encode_tensor_2d(&tmx, x, (uint64_t)d, (uint64_t)rows, d, 32, kLnRows, true)) return kErrUnsupported;
+    static std::atomic<int> sms[64] = {};
+    int n = sms[dev].load(std::memory_order_relaxed);
+    if (!n) {
+        if (cudaFuncSetAttribute(k_layernorm_seq<CW, ST, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) != cudaSuccess) return kErrCuda;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+        sms[dev].store(n, std::memory_order_relaxed);
+    }
+    const long long groups = (rows + kLnRows - 1) / kLnRows;
+    const long long grid = n < groups ? n : groups;
+    k_layernorm_seq<CW, ST, CH><<<(unsigned)grid, kLnThreads, smem, s>>>(tmx, x, y, gamma, beta, eps, d,
+                                                                        rows, device_error_word(dev));
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
 int layernorm_rows(const float* x, float* y, const float* gamma, const float* beta, float eps,
                    long long rows, int d, cudaStream_t s) {
     if (rows < 0 || d <= 0) return kErrInvalidDim;
     if (rows == 0) return kOk;
     if (!x || !y) return kErrNullPtr;
-    const long long groups = (rows + kLnRows - 1) / kLnRows;
     const bool vec = (d % 4 == 0) && al16(x) && al16(y) && (!gamma || al16(gamma)) &&
                      (!beta || al16(beta));
     if (vec) {
-        // Persistent: kLnCtasPerSm one-warp CTAs per SM, so that only that many
-        // 512 KB row groups per SM are in flight and their re-reads hit L2.
-        const int smem = (kLnRing + 2 * kLnMaxD) * (int)sizeof(float);
-        static bool attr_set[64] = {};
-        static int sms[64] = {};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 0 || dev >= 64) return kErrUnsupported;
-        if (!attr_set[dev]) {
-            if (cudaFuncSetAttribute(k_layernorm_seq, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem) != cudaSuccess) return kErrCuda;
-            cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-            if (sms[dev] <= 0) sms[dev] = 148;
-            attr_set[dev] = true;
-        }
-        int per_sm = kLnCtasPerSm;
-        if (const char* e = getenv("RAC_LN_CTAS_PER_SM")) per_sm = atoi(e) > 0 ? atoi(e) : per_sm;
-        long long grid = (long long)sms[dev] * per_sm;
-        if (grid > groups) grid = groups;
-        k_layernorm_seq<<<(unsigned)grid, 32, smem, s>>>(x, y, gamma, beta, eps, d, rows);
-    } else {
-        const long long blocks = (rows + 127) / 128;
-        if (blocks > 0x7fffffffLL) return kErrInvalidDim;
-        k_layernorm_seq_any<<<(unsigned)blocks, 128, 0, s>>>(x, y, gamma, beta, eps, d, rows);
+        // 2 chain warps, 128-column chunks, 4 stages each (measured against one chain
+        // warp with 128 x 6 / 256 x 4 rings and two with 128 x 6: 0.189-0.223 ms)
+        const int st = launch_ln<128, 4, 2>(x, y, gamma, beta, eps, d, rows, dev, s);
+        if (st != kErrUnsupported) return st;
     }
+    const long long blocks = (rows + 127) / 128;
+    if (blocks > 0x7fffffffLL) return kErrInvalidDim;
+    k_layernorm_seq_any<<<(unsigned)blocks, 128, 0, s>>>(x, y, gamma, beta, eps, d, rows);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
