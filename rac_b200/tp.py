@@ -9,8 +9,9 @@
   qkv and the FFN up-projections split by output rows (whole heads / ff
   slices per rank), out_proj and the down-projection split by input columns,
   one NCCL all-reduce (sum, fp32) after each of the two row-split GEMMs.
-  The gated FFN's gate and up shards run as one GEMM over row-interleaved
-  weights whose epilogue writes silu(gate) * up.
+  The batch runs in two pieces, so each piece's all-reduce overlaps the next
+  piece's GEMMs.  The gated FFN's gate and up shards run as one GEMM over
+  row-interleaved weights whose epilogue writes silu(gate) * up.
   Rank 0 adds the residual in its GEMM epilogue so the all-reduce yields
   x + sum of partials directly.
 """
@@ -94,25 +95,55 @@ class TPLlamaBlock(nn.Module):
             p.update(fc1=g(self.w_fc1.weight), fc2=g(self.w_fc2.weight))
         return p
 
-    def _allreduce(self, t):
+    def _allreduce(self, t, async_op: bool = False):
         if self.world > 1:
             import torch.distributed as dist
-            dist.all_reduce(t, group=self.group)
-        return t
+            return dist.all_reduce(t, group=self.group, async_op=async_op)
+        return None
 
-    @torch.no_grad()
-    def forward(self, x, mask=None, is_causal=True, positions=None):
+    def _attn_half(self, x, mask, is_causal, positions):
         res = x if self.rank == 0 else None
         ctx = self.attn._context(self.norm1(x), mask, is_causal, positions, n_heads=self.h_local)
-        h = self._allreduce(_apply(ctx, self.attn.out_proj, residual=res))
+        return _apply(ctx, self.attn.out_proj, residual=res)
+
+    def _ffn_half(self, h):
         n2 = self.norm2(h)
         res = h if self.rank == 0 else None
         if self.gated:
-            y = _apply(_apply(n2, self.w_gu, act=ext.ACT_SWIGLU), self.w_down, residual=res)
-        else:
-            t = _apply(n2, self.w_fc1, act=self.act_id)
-            y = _apply(t, self.w_fc2, residual=res)
-        return self._allreduce(y)
+            return _apply(_apply(n2, self.w_gu, act=ext.ACT_SWIGLU), self.w_down, residual=res)
+        return _apply(_apply(n2, self.w_fc1, act=self.act_id), self.w_fc2, residual=res)
+
+    @torch.no_grad()
+    def forward(self, x, mask=None, is_causal=True, positions=None, chunks: int | None = None):
+        """chunks: split the batch into this many pieces (default: 2 when world > 1
+        and the batch allows it) so that each piece's all-reduce runs on NCCL's
+        stream while the next piece's GEMMs run -- the sequences of a batch are
+        independent, so the result is the same bits as one piece."""
+        B = x.shape[0]
+        c = chunks if chunks is not None else (2 if self.world > 1 and B >= 2 else 1)
+        c = max(1, min(c, B))
+        if c == 1:
+            h = self._attn_half(x, mask, is_causal, positions)
+            self._allreduce(h)
+            y = self._ffn_half(h)
+            self._allreduce(y)
+            return y
+        hs, works = [], []
+        for xc in x.chunk(c, dim=0):
+            h = self._attn_half(xc, mask, is_causal, positions)
+            works.append(self._allreduce(h, async_op=True))
+            hs.append(h)
+        ys, works2 = [], []
+        for h, w in zip(hs, works):
+            if w is not None:
+                w.wait()                   # this stream waits for the reduced h
+            y = self._ffn_half(h)
+            works2.append(self._allreduce(y, async_op=True))
+            ys.append(y)
+        for w in works2:
+            if w is not None:
+                w.wait()
+        return torch.cat(ys, 0)
 
 
 class _ShardLinear(nn.Module):

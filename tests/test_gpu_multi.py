@@ -2,8 +2,9 @@
 
 * N-column sharded rac_matmul: each rank's columns equal the single-GPU
   result bit for bit (the per-output arithmetic is unchanged).
-* TPLlamaBlock at world 2 equals the unsharded block (CORDIC, 16 iterations)
-  within normwise 1e-4 (the all-reduce changes the summation order).
+* TPLlamaBlock at world 2 equals the unsharded block (CORDIC 16 and FAST)
+  within normwise 1e-4 (the all-reduce changes the summation order), and its
+  overlapped two-piece forward equals the one-piece forward bit for bit.
 """
 import math
 import os
@@ -48,9 +49,15 @@ def _worker(rank, world, port, q):
         x = torch.randn((2, 64, 256), generator=g).to(dev)
         with torch.no_grad():
             y_ref = full(x, is_causal=True)
-            y_tp = tp.TPLlamaBlock(full, world, rank)(x)
+            blk = tp.TPLlamaBlock(full, world, rank)
+            y_tp = blk(x)                                   # two batch pieces, overlapped
+            y_one = blk(x, chunks=1)
+            R.rac_set_mode("fast")
+            y_ref_f = full(x, is_causal=True)
+            y_tp_f = blk(x)
         err = float((y_tp - y_ref).abs().max() / y_ref.pow(2).mean().sqrt())
-        q.put((rank, ok_mm, err))
+        err_f = float((y_tp_f - y_ref_f).abs().max() / y_ref_f.pow(2).mean().sqrt())
+        q.put((rank, ok_mm, err, bool(torch.equal(y_tp, y_one)), err_f))
     finally:
         dist.destroy_process_group()
 
@@ -67,6 +74,8 @@ def test_two_rank_matmul_and_tp_block():
     res = [q.get(timeout=300) for _ in ps]
     for p in ps:
         p.join(timeout=120)
-    for rank, ok_mm, err in res:
+    for rank, ok_mm, err, same_pieces, err_f in res:
         assert ok_mm, rank
         assert err <= 1e-4, (rank, err)
+        assert err_f <= 1e-4, (rank, err_f)       # FAST mode: NN on the shards' cached W^T
+        assert same_pieces, rank                  # batch pieces: the bits of one piece
