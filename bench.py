@@ -63,6 +63,8 @@ def dist_init():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import torch.distributed as dist
+        # NCCL's banner / debug lines go to stderr: stdout carries rank 0's JSON line only
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:
@@ -706,6 +708,9 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=16384, help="norm workloads: row count")
     ap.add_argument("--log2n", type=int, default=26, help="rotate workload: log2 of the vector count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-chunks", type=int, default=None,
+                    help="llama: batch pieces per tensor-parallel forward, each piece's all-reduce "
+                         "overlapping the next piece's GEMMs (default 1)")
     ap.add_argument("--no-llama", action="store_true",
                     help="matmul workload: skip the RACLlamaBlock measurement in the same line")
     args = ap.parse_args()

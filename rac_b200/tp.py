@@ -9,8 +9,8 @@
   qkv and the FFN up-projections split by output rows (whole heads / ff
   slices per rank), out_proj and the down-projection split by input columns,
   one NCCL all-reduce (sum, fp32) after each of the two row-split GEMMs.
-  The batch runs in two pieces, so each piece's all-reduce overlaps the next
-  piece's GEMMs.  The gated FFN's gate and up shards run as one GEMM over
+  The batch can run in pieces, so each piece's all-reduce overlaps the next
+  piece's GEMMs (off by default: at TP2 it did not pay).  The gated FFN's gate and up shards run as one GEMM over
   row-interleaved weights whose epilogue writes silu(gate) * up.
   Rank 0 adds the residual in its GEMM epilogue so the all-reduce yields
   x + sum of partials directly.
@@ -115,12 +115,14 @@ class TPLlamaBlock(nn.Module):
 
     @torch.no_grad()
     def forward(self, x, mask=None, is_causal=True, positions=None, chunks: int | None = None):
-        """chunks: split the batch into this many pieces (default: 2 when world > 1
-        and the batch allows it) so that each piece's all-reduce runs on NCCL's
-        stream while the next piece's GEMMs run -- the sequences of a batch are
-        independent, so the result is the same bits as one piece."""
+        """chunks: split the batch into this many pieces so that each piece's
+        all-reduce runs on NCCL's stream while the next piece's GEMMs run (the
+        sequences of a batch are independent; at world 2 the result is the same
+        bits as one piece).  Default 1: at TP2 in FAST mode the two all-reduces
+        cost ~1 % of the step and halving the GEMMs' M cost more (32.3 ms with
+        2 pieces, 33.7 with 4, 31.9 with 1)."""
         B = x.shape[0]
-        c = chunks if chunks is not None else (2 if self.world > 1 and B >= 2 else 1)
+        c = chunks if chunks is not None else 1
         c = max(1, min(c, B))
         if c == 1:
             h = self._attn_half(x, mask, is_causal, positions)
@@ -238,8 +240,9 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(99)
     x = torch.randn((Bt, T, d), device=dev, generator=g)
+    chunks = getattr(args, "tp_chunks", None)
     for _ in range(args.warmup):
-        blk(x)
+        blk(x, chunks=chunks)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -251,7 +254,7 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             starts[i].record(s)
-            y = blk(x)
+            y = blk(x, chunks=chunks)
             ends[i].record(s)
         torch.cuda.synchronize()
     launches = _lib.CALLS["n"] - calls0
@@ -267,7 +270,7 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
         barrier(world)
         t0 = time.perf_counter()
         xd = xh.to(dev, non_blocking=True)
-        yh.copy_(blk(xd), non_blocking=True)
+        yh.copy_(blk(xd, chunks=chunks), non_blocking=True)
         torch.cuda.synchronize()
         ts.append(time.perf_counter() - t0)
     te = max_over_ranks(statistics.mean(ts), world)
@@ -290,7 +293,8 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
         "data": "synthetic (random-init weights ~N(0,0.02))",
         "config": {"workload": f"RACLlamaBlock d={d} H={H} ff={ff} SwiGLU, x [{Bt},{T},{d}], causal, "
                                f"{args.mode} {args.iters if args.mode == 'cordic' else ''}",
-                   "parallelism": f"tp{world}", "l2": "inputs and weights larger than L2"},
+                   "parallelism": f"tp{world}", "l2": "inputs and weights larger than L2",
+                   "tp_batch_pieces": chunks if chunks is not None else 1},
         "roofline": {"bound": "fp32_issue", "achieved": macs / (t_local * 1e-3) / 1e12,
                      "peak": peak_mac / 1e12, "unit": "TMAC/s (projection GEMMs only)",
                      "frac": macs / (t_local * 1e-3) / peak_mac, "traffic": None},

@@ -50,8 +50,8 @@ def _worker(rank, world, port, q):
         with torch.no_grad():
             y_ref = full(x, is_causal=True)
             blk = tp.TPLlamaBlock(full, world, rank)
-            y_tp = blk(x)                                   # two batch pieces, overlapped
-            y_one = blk(x, chunks=1)
+            y_tp = blk(x, chunks=2)                         # two batch pieces, overlapped
+            y_one = blk(x)
             R.rac_set_mode("fast")
             y_ref_f = full(x, is_causal=True)
             y_tp_f = blk(x)
