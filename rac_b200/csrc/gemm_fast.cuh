@@ -165,4 +165,14 @@ int launch_fast_tma(const GemmParams& p_in, cudaStream_t s) {
 #define RACB_FAST_TMA_INST(LAYOUT, V) template int launch_fast_tma<LAYOUT, V>(const GemmParams&, cudaStream_t);
 #define RACB_FAST_TMA_EXTERN(LAYOUT, V) extern template int launch_fast_tma<LAYOUT, V>(const GemmParams&, cudaStream_t);
 
+// NT (B = an nn.Linear weight [N, K]): its tiles would land n-major, where the
+// FFMA2 pairs along n cost a register move per pair; a TMA kernel on 128-byte
+// swizzled k-major tiles measured 32.5 TFLOP/s at 4096^3 against 37.3 for the
+// general kernel.  Instead B is transposed once per call into a pooled buffer
+// (2 x |B| bytes of traffic, ~0.3 % of the GEMM at the RACLinear shapes) and
+// the NN kernel runs on it -- the same fma sequence per output, so the same bits.
+__global__ void k_transpose_f32(const float* __restrict__ src, long long lds, float* __restrict__ dst,
+                                long long ldd, int rows, int cols);
+int launch_fast_tma_nt(const GemmParams& p_in, cudaStream_t s);
+
 }  // namespace racb
