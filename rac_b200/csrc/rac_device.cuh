@@ -211,6 +211,53 @@ __device__ __forceinline__ bool cordic_rotate_scaled(float& xr, float& yr, float
     return ok;
 }
 
+// Two independent rotations at once: the prologue per vector as above, then
+// the micro-rotations of both vectors as packed pairs -- the x, y and angle
+// updates of the two vectors are three FFMA2 (two FMAs each, each rounded
+// once: the bits of the scalar form) instead of six FFMA, with the two
+// directions from one LOP3 each.
+template <int ITERS>
+__device__ __forceinline__ bool cordic_rotate_scaled_x2(float& xa, float& ya, float& xb, float& yb,
+                                                        float vxa, float vya, float vxb, float vyb,
+                                                        float kinv, float tha, float thb,
+                                                        unsigned sign_mask = 0x80000000u) {
+    bool ok = true;
+    float ang[2], px[2], py[2];
+    const float th2[2] = {tha, thb}, vx2[2] = {vxa, vxb}, vy2[2] = {vya, vyb};
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+        float theta = th2[v];
+        if (fabsf(theta) >= kPi) {
+            const float TAU = 2.0f * kPi;
+            int w = 0;
+            while (theta > kPi) { theta = __fsub_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+            while (theta <= -kPi) { theta = __fadd_rn(theta, TAU); if (++w >= kWrapLimit) { ok = false; break; } }
+        }
+        const bool fold = fabsf(theta) > kPi * 0.5f;
+        const float c = fold ? __uint_as_float((~__float_as_uint(theta) & sign_mask) | __float_as_uint(kPi))
+                             : 0.0f;
+        ang[v] = fmaxf(__fadd_rn(theta, c), -INFINITY);
+        const float ks = fold ? -kinv : kinv;
+        px[v] = __fmul_rn(vx2[v], ks);
+        py[v] = __fmul_rn(vy2[v], ks);
+    }
+    float2 X = make_float2(px[0], px[1]), Y = make_float2(py[0], py[1]), A = make_float2(ang[0], ang[1]);
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+        unsigned da, db;
+        asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(da) : "r"(__float_as_uint(A.x)), "r"(sign_mask), "r"(pow2neg_bits(i)));
+        asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(db) : "r"(__float_as_uint(A.y)), "r"(sign_mask), "r"(pow2neg_bits(i)));
+        const float2 DS = make_float2(__uint_as_float(da), __uint_as_float(db));
+        const float2 NDS = make_float2(-DS.x, -DS.y);
+        const float2 Xn = __ffma2_rn(NDS, Y, X);
+        Y = __ffma2_rn(DS, X, Y);
+        X = Xn;
+        if (i + 1 < ITERS) A = __ffma2_rn(NDS, make_float2(atan_scaled(i), atan_scaled(i)), A);
+    }
+    xa = X.x; xb = X.y; ya = Y.x; yb = Y.y;
+    return ok;
+}
+
 // The same rotation of an already scaled (x, y).
 template <int ITERS>
 __device__ __forceinline__ bool cordic_rotate(float& xr, float& yr, float theta,

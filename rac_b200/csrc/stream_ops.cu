@@ -89,10 +89,17 @@ __global__ void __launch_bounds__(256) k_rotate(const float2* __restrict__ v,
                 tn = __ldcs(reinterpret_cast<const float4*>(th) + q + stride);
             }
             float x0, y0, x1, y1, x2, y2, x3, y3;
-            ok &= rotate_one<ITERS>(x0, y0, v01.x, v01.y, k_inv, t.x, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x1, y1, v01.z, v01.w, k_inv, t.y, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x2, y2, v23.x, v23.y, k_inv, t.z, iters, sign_mask);
-            ok &= rotate_one<ITERS>(x3, y3, v23.z, v23.w, k_inv, t.w, iters, sign_mask);
+            if constexpr (ITERS > 0) {                // two vectors per packed rotation
+                ok &= cordic_rotate_scaled_x2<ITERS>(x0, y0, x1, y1, v01.x, v01.y, v01.z, v01.w,
+                                                     k_inv, t.x, t.y, sign_mask);
+                ok &= cordic_rotate_scaled_x2<ITERS>(x2, y2, x3, y3, v23.x, v23.y, v23.z, v23.w,
+                                                     k_inv, t.z, t.w, sign_mask);
+            } else {
+                ok &= rotate_one<ITERS>(x0, y0, v01.x, v01.y, k_inv, t.x, iters, sign_mask);
+                ok &= rotate_one<ITERS>(x1, y1, v01.z, v01.w, k_inv, t.y, iters, sign_mask);
+                ok &= rotate_one<ITERS>(x2, y2, v23.x, v23.y, k_inv, t.z, iters, sign_mask);
+                ok &= rotate_one<ITERS>(x3, y3, v23.z, v23.w, k_inv, t.w, iters, sign_mask);
+            }
             __stcs(reinterpret_cast<float4*>(out) + 2 * q, make_float4(x0, y0, x1, y1));
             __stcs(reinterpret_cast<float4*>(out) + 2 * q + 1, make_float4(x2, y2, x3, y3));
         }
