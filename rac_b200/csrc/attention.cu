@@ -160,11 +160,13 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
     // l = l * alpha + sum e, O = O * alpha + e V (keys ascending).
     float mrow[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     float lsum[4] = {0.f, 0.f, 0.f, 0.f};
-    float4 o[4][CG];
+    // O accumulators as packed pairs (columns 4c, 4c+1 and 4c+2, 4c+3): the
+    // P V update is FFMA2, two FMAs per instruction, each rounded once.
+    float2 o[4][CG][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int g = 0; g < CG; ++g) o[i][g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int g = 0; g < CG; ++g) o[i][g][0] = o[i][g][1] = make_float2(0.f, 0.f);
     for (int kb = 0; kb < nkb; ++kb) {
         // V(kb) streams in during the scores and softmax of tile kb.
         load_tile_async<HD, false>(Vs, vh, kb * kAttBK, seq);
@@ -184,10 +186,11 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
             const float alpha = (mn == -INFINITY) ? 1.0f : expf(__fsub_rn(mrow[i], mn));
             mrow[i] = mn;
             lsum[i] = __fmul_rn(lsum[i], alpha);
+            const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
-                o[i][g].x = __fmul_rn(o[i][g].x, alpha); o[i][g].y = __fmul_rn(o[i][g].y, alpha);
-                o[i][g].z = __fmul_rn(o[i][g].z, alpha); o[i][g].w = __fmul_rn(o[i][g].w, alpha);
+                o[i][g][0] = __fmul2_rn(o[i][g][0], a2);
+                o[i][g][1] = __fmul2_rn(o[i][g][1], a2);
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -207,15 +210,17 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
         __syncthreads();
         const int kmax = min(kAttBK, seq - kb * kAttBK);
         auto pv_key = [&](int s, const float (&p)[4]) {
+            float2 pd[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pd[i] = make_float2(p[i], p[i]);
 #pragma unroll
             for (int g = 0; g < CG; ++g) {
                 const float4 vv = *reinterpret_cast<const float4*>(Vs + s * HD + cg * 4 + 32 * g);
+                const float2 v01 = make_float2(vv.x, vv.y), v23 = make_float2(vv.z, vv.w);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    o[i][g].x = __fmaf_rn(p[i], vv.x, o[i][g].x);
-                    o[i][g].y = __fmaf_rn(p[i], vv.y, o[i][g].y);
-                    o[i][g].z = __fmaf_rn(p[i], vv.z, o[i][g].z);
-                    o[i][g].w = __fmaf_rn(p[i], vv.w, o[i][g].w);
+                    o[i][g][0] = __ffma2_rn(pd[i], v01, o[i][g][0]);
+                    o[i][g][1] = __ffma2_rn(pd[i], v23, o[i][g][1]);
                 }
             }
         };
@@ -253,9 +258,9 @@ k_attention(const float* __restrict__ q, const float* __restrict__ k, const floa
                         : (lsum[i] > 0.0f ? __fdiv_rn(1.0f, lsum[i]) : 0.0f);
 #pragma unroll
         for (int g = 0; g < CG; ++g) {
-            const float4 r = o[i][g];
+            const float2 r0 = o[i][g][0], r1 = o[i][g][1];
             *reinterpret_cast<float4*>(oh + (long long)t * HD + cg * 4 + 32 * g) =
-                make_float4(__fmul_rn(r.x, inv), __fmul_rn(r.y, inv), __fmul_rn(r.z, inv), __fmul_rn(r.w, inv));
+                make_float4(__fmul_rn(r0.x, inv), __fmul_rn(r0.y, inv), __fmul_rn(r1.x, inv), __fmul_rn(r1.y, inv));
         }
     }
 }
