@@ -11,7 +11,7 @@ namespace racb {
 RACB_FAST_TMA_EXTERN(kNN, 1) RACB_FAST_TMA_EXTERN(kTN, 1) RACB_FAST_TMA_EXTERN(kNN, 2) RACB_FAST_TMA_EXTERN(kTN, 2)
 
 // FAST mode on operands that meet the TMA rules and no split-K: the
-// TMA-staged FFMA2 kernels (gemm_fast.cuh) -- NN / TN with 64 x 128 tiles (or
+// TMA-staged FFMA2 kernels (gemm_fast.cuh) -- NN / TN with 64 x 128 x 32 tiles (or
 // 128 x 128 when variant bit 0x2000 asks), NT with swizzled k-major tiles
 // (not with the SwiGLU epilogue).  Everything else (unaligned operands,
 // split-K, variant bit 0x400) runs the general kernel.
@@ -20,6 +20,7 @@ static int pick_fast_tma(const GemmParams& p, int layout, int variant, cudaStrea
     if (layout == kNT) return launch_fast_tma_nt(p, s);
     if (variant & 0x2000)
         return layout == kNN ? launch_fast_tma<kNN, 1>(p, s) : launch_fast_tma<kTN, 1>(p, s);
+
     return layout == kNN ? launch_fast_tma<kNN, 2>(p, s) : launch_fast_tma<kTN, 2>(p, s);
 }
 

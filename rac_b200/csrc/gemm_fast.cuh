@@ -13,7 +13,7 @@
 //  * TMA staging through a 4-deep mbarrier ring takes the global loads off the
 //    compute warps (with FFMA2 alone, register staging left the kernel
 //    waiting on global loads: 3.1-3.4 ms at 4096^3).
-// Measured at 4096^3 NN: 2.47 ms, 55.7 TFLOP/s (FP32 pipe 75-78 % busy;
+// Measured at 4096^3 NN: 2.37 ms, 58.1 TFLOP/s (0.78 of the FP32 FMA peak;
 // cuBLAS SGEMM 63.4 TFLOP/s on the same GPU).
 #pragma once
 #include "gemm_kernel.cuh"
@@ -132,11 +132,13 @@ k_gemm_fast_tma(const __grid_constant__ GemmParams p) {
 }
 
 // TMA tile shapes of the FAST kernel: 1: 128 x 128 x 16, 256 threads, 4 stages
-// (64 KB), 2 CTAs per SM -- 2.56 ms at 4096^3; 2 (the default): 64 x 128 x 16,
-// 128 threads, 4 stages (48 KB), 3 CTAs per SM -- 2.47 ms.
+// (64 KB), 2 CTAs per SM -- 2.53-2.56 ms at 4096^3; 2 (the default): 64 x 128 x
+// 32, 128 threads, 3 stages (72 KB), 3 CTAs per SM -- 2.37 ms (58.1 TFLOP/s;
+// 8192^3: 59.4).  Also measured: 64 x 128 x 16 with 4 stages 2.44-2.47 ms,
+// 128 x 128 x 16 with 3 stages 2.53, 128 x 64 x 16 with 4 stages 2.45.
 template <int V> struct FastTmaCfg;
 template <> struct FastTmaCfg<1> { static constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8, ST = 4, MINB = 2; };
-template <> struct FastTmaCfg<2> { static constexpr int BM = 64, BN = 128, BK = 16, TM = 8, TN = 8, ST = 4, MINB = 3; };
+template <> struct FastTmaCfg<2> { static constexpr int BM = 64, BN = 128, BK = 32, TM = 8, TN = 8, ST = 3, MINB = 3; };
 
 
 template <int LAYOUT, int V>
