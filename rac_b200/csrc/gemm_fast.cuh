@@ -16,6 +16,8 @@
 // Measured at 4096^3 NN: 2.37 ms, 58.1 TFLOP/s (0.78 of the FP32 FMA peak;
 // cuBLAS SGEMM 63.4 TFLOP/s on the same GPU).
 #pragma once
+#include <atomic>
+
 #include "gemm_kernel.cuh"
 
 namespace racb {
@@ -149,14 +151,14 @@ int launch_fast_tma(const GemmParams& p_in, cudaStream_t s) {
     GemmParams p = p_in;
     if (p.ws || !make_tensor_maps(p, LAYOUT, T::BM, T::BN, T::BK)) return kErrUnsupported;
     auto kern = k_gemm_fast_tma<LAYOUT, T::BM, T::BN, T::BK, T::TM, T::TN, T::ST, T::MINB>;
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};          // per device; setting it twice is harmless
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return kErrUnsupported;
-    if (!attr[dev]) {
+    if (!attr[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
             return kErrCuda;
-        attr[dev] = true;
+        attr[dev].store(true, std::memory_order_release);
     }
     dim3 grid((p.M + T::BM - 1) / T::BM, (p.N + T::BN - 1) / T::BN, 1);
     if (grid.y > 65535) return kErrInvalidDim;
