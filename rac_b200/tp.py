@@ -261,16 +261,30 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
     barrier(world)
     t_local = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
     t = max_over_ranks(t_local, world)
-    # e2e: pinned host input -> device, forward, result back to the host.
-    xh = x.cpu().pin_memory()
+    # e2e: pinned host input -> device, forward, result back to the host.  With
+    # several ranks each uploads one 1/world slice of the token rows over its own
+    # PCIe link, NCCL all-gathers the slices over NVLink, and each rank downloads
+    # its slice of the (replicated) output: together they move x in and y out
+    # once instead of once per rank.
+    rows = Bt * T
+    r0, r1 = rows * rank // world, rows * (rank + 1) // world
+    even = rows % world == 0
+    x2 = x.reshape(rows, d)
+    xh = (x2[r0:r1] if (world > 1 and even) else x2).cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
+    xfull = torch.empty((rows, d), device=dev) if (world > 1 and even) else None
     ts = []
     for _ in range(max(1, min(args.steps, 3))):
         torch.cuda.synchronize()
         barrier(world)
         t0 = time.perf_counter()
-        xd = xh.to(dev, non_blocking=True)
-        yh.copy_(blk(xd, chunks=chunks), non_blocking=True)
+        if xfull is not None:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(xfull, xh.to(dev, non_blocking=True))
+            yd = blk(xfull.view(Bt, T, d), chunks=chunks).reshape(rows, d)[r0:r1]
+        else:
+            yd = blk(xh.to(dev, non_blocking=True).view(Bt, T, d), chunks=chunks).reshape(rows, d)
+        yh.copy_(yd, non_blocking=True)
         torch.cuda.synchronize()
         ts.append(time.perf_counter() - t0)
     te = max_over_ranks(statistics.mean(ts), world)
@@ -299,7 +313,9 @@ def bench_llama(args, world, rank, local, barrier, max_over_ranks, ClockSampler)
                      "peak": peak_mac / 1e12, "unit": "TMAC/s (projection GEMMs only)",
                      "frac": macs / (t_local * 1e-3) / peak_mac, "traffic": None},
         "e2e": {"value": tokens / te, "unit": "tokens/s", "h2d_bytes_per_step": 4 * x.numel(),
-                "d2h_bytes_per_step": 4 * x.numel()},
+                "d2h_bytes_per_step": 4 * x.numel(),
+                "note": "bytes summed over ranks: with N > 1 each rank uploads and downloads "
+                        "1/N of the token rows; the input slices are all-gathered over NVLink"},
         "gpu_launches": launches,
         "gpu_launches_note": "librac_b200 entry-point calls in the timed region (projections, "
                              "fused attention, RMSNorm, RoPE)",
