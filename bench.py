@@ -455,6 +455,32 @@ def run_matmul(args, world, rank, local) -> dict | None:
     _lib.check()
     te = max_over_ranks(statistics.mean(ts), world)
     assert torch.equal(Ch, C.cpu()), "e2e result differs from the device-resident run"
+    te_abi = te
+    # With N > 1 ranks the replicated A need not cross every rank's PCIe link:
+    # through rac_b200.tp each rank uploads 1/N of A's rows and its B block, NCCL
+    # all-gathers A over NVLink, and each rank downloads its C block.
+    te_dist = None
+    if world > 1 and M % world == 0:
+        import torch.distributed as dist
+        from rac_b200 import tp
+        a0, a1 = M * rank // world, M * (rank + 1) // world
+        Ash = A[a0:a1].cpu().pin_memory()
+        Afull = torch.empty((M, K), device=dev)
+        Cd = torch.empty((M, Nl), device=dev)
+        ts = []
+        for it_ in range(e2e_steps + 1):
+            torch.cuda.synchronize()
+            barrier(world)
+            t0 = time.perf_counter()
+            dist.all_gather_into_tensor(Afull, Ash.to(dev, non_blocking=True))
+            tp.sharded_matmul(Afull, Bh.to(dev, non_blocking=True), iters, mode, out=Cd)
+            Ch.copy_(Cd, non_blocking=True)
+            torch.cuda.synchronize()
+            if it_:
+                ts.append(time.perf_counter() - t0)
+        te_dist = max_over_ranks(statistics.mean(ts), world)
+        assert torch.equal(Ch, C.cpu()), "distributed e2e result differs from the device-resident run"
+        te = min(te, te_dist)
 
     # Context: cuBLAS SGEMM (torch.matmul, fp32, TF32 off) on the same operands.
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -486,8 +512,16 @@ def run_matmul(args, world, rank, local) -> dict | None:
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
         "roofline": roofline_fp32(achieved_local, iters, peaks, sms, t_local, traffic, mode),
         "e2e": {"value": 2.0 * M * N * K / te / 1e9, "unit": "GOP/s",
-                "h2d_bytes_per_step": 4 * (M * K + K * Nl), "d2h_bytes_per_step": 4 * M * Nl,
-                "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"},
+                "h2d_bytes_per_step": 4 * (M * K + K * Nl) if te_dist is None or te_abi <= te_dist
+                else 4 * (M * K // world + K * Nl),
+                "d2h_bytes_per_step": 4 * M * Nl,
+                "api": "rac_matmul_ex (C ABI), pinned host buffers, blocking"
+                       if te_dist is None or te_abi <= te_dist else
+                       "rac_b200.tp: 1/N of A's rows and this rank's B block uploaded from pinned host "
+                       "buffers, A all-gathered over NVLink (NCCL), sharded_matmul, C block downloaded",
+                "c_abi_value": 2.0 * M * N * K / te_abi / 1e9,
+                "nccl_gather_value": None if te_dist is None else 2.0 * M * N * K / te_dist / 1e9,
+                "bytes_note": "per rank"},
         "context": {"cublas_sgemm": {"value": 2.0 * M * Nl * K / (t_cublas * 1e-3) / 1e9,
                                      "unit": "GFLOP/s", "ms": t_cublas,
                                      "note": "torch.matmul fp32 (TF32 off) on this rank's operands; "
