@@ -274,6 +274,21 @@ k_gemm(const __grid_constant__ GemmParams p) {
                 sgn[j] = __float_as_uint(b[j]) & 0x80000000u;
                 mag[j] = __uint_as_float(__float_as_uint(b[j]) & 0x7FFFFFFFu);
             }
+            if constexpr (ITERS > 0 && (TM % 2) == 0) {
+                // two rows' micro-rotations per FFMA2
+                const float2 ki2 = make_float2(k_inv, k_inv);
+#pragma unroll
+                for (int j = 0; j < TN; ++j) {
+#pragma unroll
+                    for (int i = 0; i < TM; i += 2) {
+                        const float2 sa = make_float2(__uint_as_float(__float_as_uint(a[i]) ^ sgn[j]),
+                                                      __uint_as_float(__float_as_uint(a[i + 1]) ^ sgn[j]));
+                        const float2 xs = __fmul2_rn(gemm_cordic_x2<ITERS>(sa), ki2);
+                        acc[i][j] = __fmaf_rn(xs.x, mag[j], acc[i][j]);
+                        acc[i + 1][j] = __fmaf_rn(xs.y, mag[j], acc[i + 1][j]);
+                    }
+                }
+            } else {
 #pragma unroll
             for (int j = 0; j < TN; ++j) {
 #pragma unroll
@@ -284,6 +299,7 @@ k_gemm(const __grid_constant__ GemmParams p) {
                     else                     x = gemm_cordic_x_rt(sa, p.iters, p.coef);
                     acc[i][j] = __fmaf_rn(__fmul_rn(x, k_inv), mag[j], acc[i][j]);
                 }
+            }
             }
         }
     };

@@ -125,6 +125,32 @@ __device__ __forceinline__ float gemm_cordic_x(float sa) {
     }
 }
 
+// gemm_cordic_x for two independent operands at once: the same micro-
+// rotations as packed FFMA2 (each half one fused multiply-add, rounded once:
+// the bits of the scalar form).
+template <int ITERS>
+__device__ __forceinline__ float2 gemm_cordic_x2(float2 sa) {
+    if constexpr (ITERS <= 1) {
+        return sa;
+    } else {
+        float2 x = __ffma2_rn(make_float2(-gemm_coef(1), -gemm_coef(1)), sa, sa);
+        float2 ys = sa;
+#pragma unroll
+        for (int t = 2; t < ITERS; ++t) {
+            const float c = gemm_coef(t);
+            const float2 c1 = make_float2(-0.5f * c, -0.5f * c), c2 = make_float2(2.0f * c, 2.0f * c);
+            if (t == ITERS - 1) {
+                x = __ffma2_rn(c1, ys, x);
+            } else {
+                const float2 xn = __ffma2_rn(c1, ys, x);
+                ys = __ffma2_rn(c2, x, ys);
+                x = xn;
+            }
+        }
+        return x;
+    }
+}
+
 // Runtime-iteration variant (any n in [1, 24]); coefficients come from a
 // kernel-argument table.
 __device__ __forceinline__ float gemm_cordic_x_rt(float sa, int iters,
