@@ -343,6 +343,63 @@ def hip_gemm(A, B, layout: str = "nn", mode: int = 1, iters: int = 16):
     return C_
 
 
+# ── the reference decoder bench's safetensors reader ───────────────────────
+
+ST_PATH = os.path.join(HERE, "_ref", "libst_ref.so")
+_st = None
+
+
+def st_available() -> bool:
+    return os.path.exists(ST_PATH)
+
+
+class _StTensor(C.Structure):
+    # bench/safetensors_reader.h: st_tensor (ST_MAX_NAME 256, ST_MAX_NDIM 8)
+    _fields_ = [("name", C.c_char * 256), ("dtype", C.c_int), ("ndim", C.c_int),
+                ("shape", C.c_int64 * 8), ("offset", C.c_size_t), ("nbytes", C.c_size_t)]
+
+
+def ref_read_safetensors(path: str) -> dict:
+    """Every tensor of a file through the reference reader (st_open, st_find,
+    st_to_f32), as float32 arrays of the recorded shape."""
+    global _st
+    if _st is None:
+        lib = C.CDLL(ST_PATH, mode=os.RTLD_LOCAL | os.RTLD_NOW)
+        lib.st_open.argtypes = [C.c_char_p, C.c_char_p]
+        lib.st_open.restype = C.c_void_p
+        lib.st_close.argtypes = [C.c_void_p]
+        lib.st_find.argtypes = [C.c_void_p, C.c_char_p]
+        lib.st_find.restype = C.POINTER(_StTensor)
+        lib.st_numel.argtypes = [C.POINTER(_StTensor)]
+        lib.st_numel.restype = C.c_size_t
+        lib.st_to_f32.argtypes = [C.c_void_p, C.POINTER(_StTensor), _fp]
+        lib.st_to_f32.restype = C.c_int
+        _st = lib
+    import json
+    import struct
+    with open(path, "rb") as f:
+        (hlen,) = struct.unpack("<Q", f.read(8))
+        names = [k for k in json.loads(f.read(hlen)) if k != "__metadata__"]
+    err = C.create_string_buffer(256)
+    h = _st.st_open(path.encode(), err)
+    if not h:
+        raise RuntimeError(err.value.decode())
+    try:
+        out = {}
+        for n in names:
+            t = _st.st_find(h, n.encode())
+            if not t:
+                raise KeyError(n)
+            shape = [t.contents.shape[i] for i in range(t.contents.ndim)]
+            a = np.empty(int(_st.st_numel(t)), np.float32)
+            if _st.st_to_f32(h, t, _p(a)) != 0:
+                raise ValueError(f"{n}: dtype not convertible")
+            out[n] = a.reshape(shape)
+        return out
+    finally:
+        _st.st_close(h)
+
+
 # ── reference-library front-ends ───────────────────────────────────────────
 
 def ref_rotate_batch(v, theta):

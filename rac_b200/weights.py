@@ -63,7 +63,8 @@ def write_safetensors(path: str, tensors: dict[str, np.ndarray], dtype: str = "F
         if dtype == "F32":
             b = a.tobytes()
         elif dtype == "F16":
-            b = a.astype(np.float16).tobytes()
+            with np.errstate(over="ignore"):    # beyond the F16 range: inf, as IEEE rounding gives
+                b = a.astype(np.float16).tobytes()
         elif dtype == "BF16":
             u = a.view(np.uint32).astype(np.uint64)
             u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16

@@ -139,3 +139,39 @@ def test_llama_layer_on_gpu_matches_transformers(tmp_path, cuda, mode, tol):
     scale = want.abs().max().item()
     assert (y - want).abs().max().item() < tol * scale
     assert (y_g - want).abs().max().item() < tol * scale
+
+
+@pytest.mark.skipif(not __import__("oracle").st_available(),
+                    reason="oracle/_ref/libst_ref.so not built (no reference checkout)")
+@pytest.mark.parametrize("dtype", ["F32", "F16", "BF16"])
+def test_reader_equals_reference_reader(tmp_path, dtype):
+    """rac_b200.weights.read_safetensors against the reference decoder bench's own
+    reader (bench/safetensors_reader.c, compiled from the reference checkout by
+    oracle/Makefile): same names, shapes and float32 bits for every tensor, F32 /
+    F16 / BF16, on random values plus zeros, signed zeros, subnormal and
+    out-of-range magnitudes, infinities and NaN; and a Llama layer loaded from
+    the reference reader's tensors equals the one loaded from ours."""
+    import oracle as O
+    rng = np.random.default_rng(len(dtype))
+    edge = np.array([0.0, -0.0, 1.0, -1.0, 1e-6, -3e-8, 6e-5, 65504.0, 1e5, -1e-40,
+                     3e38, np.inf, -np.inf, np.nan, 0.333333], np.float32)
+    tensors = {"edge": edge, "vec": rng.standard_normal(37).astype(np.float32),
+               "mat": (rng.standard_normal((16, 24)) * 0.05).astype(np.float32)}
+    cfg, layer, _ = _hf_layer()
+    prefix = "model.layers.0."
+    for name, p in layer.state_dict().items():
+        tensors[prefix + name] = p.numpy()
+    path = str(tmp_path / f"w_{dtype}.safetensors")
+    W.write_safetensors(path, tensors, dtype)
+    ours = W.read_safetensors(path)
+    theirs = O.ref_read_safetensors(path)
+    assert sorted(ours) == sorted(theirs)
+    for k in ours:
+        a, b = ours[k], theirs[k]
+        assert a.shape == b.shape, k
+        same = (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+        assert same.all(), (k, a[~same][:4], b[~same][:4])
+    blk_a = W.load_llama_layer(ours, 0, cfg.num_attention_heads, cfg.num_key_value_heads, device="cpu")
+    blk_b = W.load_llama_layer(theirs, 0, cfg.num_attention_heads, cfg.num_key_value_heads, device="cpu")
+    for (na, pa), (nb, pb) in zip(blk_a.state_dict().items(), blk_b.state_dict().items()):
+        assert na == nb and torch.equal(pa, pb), na
