@@ -63,8 +63,6 @@ def dist_init():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import torch.distributed as dist
-        # NCCL's banner / debug lines go to stderr: stdout carries rank 0's JSON line only
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:
@@ -754,6 +752,14 @@ def main() -> None:
         run_reference(args)
         return
     _all_host_threads()
+    # stdout carries rank 0's JSON line only: with several ranks, whatever the
+    # communication libraries print at start-up (NCCL's version banner) goes to
+    # stderr, and the line is written to the saved stdout descriptor.
+    json_fd = 1
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        sys.stdout.flush()
+        json_fd = os.dup(1)
+        os.dup2(2, 1)
     world, rank, local = dist_init()
     from rac_b200 import tp
     llama = None
@@ -778,7 +784,7 @@ def main() -> None:
                 llama["cpu_baseline"] = cpu_llama_baseline(sample)
             if llama is not out:
                 out["llama"] = llama
-        print(json.dumps(out))
+        os.write(json_fd, (json.dumps(out) + "\n").encode())
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
