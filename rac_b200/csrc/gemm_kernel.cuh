@@ -11,14 +11,16 @@
 //
 // The CORDIC MAC costs 2*iters FP32/INT instructions (1 LOP3 for the fold,
 // 2*iters-3 FFMA for iterations 1..iters-1 -- iteration 0 is an exact copy --
-// 1 FMUL, 1 FFMA), so the kernel is bound by the SM's FP32 issue rate, not
-// by memory: a 64x128 tile with K=4096 moves 3 MB from L2 for ~5e9 issued
-// instructions.  The design therefore spends its effort on issue efficiency:
-// an 8x8 register tile per thread gives 64 independent rotation chains for
-// the scheduler to interleave, operands are staged through shared memory
-// with a register double buffer so loads never sit on the issue path, and
-// each output accumulates sequentially over k (the reference kernels'
-// order), which keeps the result bit-identical to the CPU restatement.
+// 1 FMUL, 1 FFMA), so the kernel is bound by the SM's FP32 pipe, not by
+// memory: a 64x128 tile with K=4096 moves 3 MB from L2 for ~5e9 FP32
+// operations.  The design therefore spends its effort on keeping that pipe
+// fed: a register tile per thread gives 32-64 independent rotation chains for
+// the scheduler to interleave, the fixed-n kernels run the micro-rotations of
+// two rows as one FFMA2 (half the issue slots, so issue is no longer the
+// limit), operands are staged through shared memory by TMA (or a register
+// double buffer) so loads never sit on the issue path, and each output
+// accumulates sequentially over k (the reference kernels' order), which keeps
+// the result bit-identical to the CPU restatement.
 // No tensor cores: the defining arithmetic is the micro-rotation, not a MAC.
 #pragma once
 #include "rac_device.cuh"
